@@ -1,0 +1,360 @@
+#!/usr/bin/env python
+"""Throughput of the README ``build_model()`` training step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--widened]
+
+One step = forward + MSE loss + backward (the 19 custom ops) + gradient
+averaging across ranks + Adam, on a fixed synthetic batch of 256 images per
+GPU (input ~U(0,1) [256,64,64,3], targets ~U(0,1) [256,8,8,8], fixed seed,
+random-init weights).  For N > 1 run under torchrun: one process per GPU,
+NCCL, weak scaling (256 images per GPU).
+
+Reported (one JSON line from rank 0):
+  value     images/s over all ranks, inputs already in HBM, the step replayed
+            from one CUDA graph; per-step CUDA events, L2 flushed (256 MiB
+            write) between steps outside the timed events, max over ranks;
+  e2e       the same metric through the public API with the batch copied from
+            pinned host memory every step and the loss copied back;
+  roofline  the op with the largest share of the step, timed alone with CUDA
+            events (L2 flushed before each repetition) against its algorithmic
+            bytes / FLOPs; per_op has every op type;
+  cpu_baseline  the reference's own kernels (kernels/*.cl compiled for the host,
+            oracle/_ref) running the same step on all host cores, on a bounded
+            sample of the batch.
+``--impl reference`` times only that CPU implementation (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "opencl-tensorflow_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "build_model train images/s at 1/2/4/8 B200; per-op % of HBM/TC roofline"
+PER_GPU_BATCH = 256
+
+
+def workload(widened: bool) -> dict:
+    if widened:
+        return {"workload": "README build_model training step, widened: input 256x256x3, filters 96/192/288, "
+                            "Dense 512, head 8x8x8 -> 16x16x8; fwd+bwd+Adam(1e-3), MSE",
+                "batch_per_gpu": 128, "in_hw": 256, "out_hw": 16}
+    return {"workload": "README build_model training step: input 64x64x3, conv 48 (3,7)/(1,2), dsconv 96 and 144 "
+                        "stride 2, Dense 128, head 4x4x8 -> 8x8x8; fwd+bwd+Adam(1e-3), MSE",
+            "batch_per_gpu": PER_GPU_BATCH, "in_hw": 64, "out_hw": 8}
+
+
+def make_batch(n, in_hw, out_hw, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(0, 1, (n, in_hw, in_hw, 3)).astype(np.float32)
+    t = rng.uniform(0, 1, (n, out_hw, out_hw, 8)).astype(np.float32)
+    return x, t
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) of the GPUs in use during the timed region."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = set(uuids)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="b2_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            f = [s.strip() for s in line.split(",")]
+            if len(f) < 8:
+                continue
+            uuid = f[0]
+            if self.uuids and not any(u in uuid or uuid in u for u in self.uuids):
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------- reference (CPU)
+
+def adam_np(params, grads, state, lr=1e-3, b1=0.9, b2=0.999, eps=1e-7):
+    state["t"] = state.get("t", 0) + 1
+    t = state["t"]
+    for k, p in params.items():
+        g = grads[k]
+        m = state.setdefault(("m", k), np.zeros_like(p))
+        v = state.setdefault(("v", k), np.zeros_like(p))
+        m *= b1
+        m += (1 - b1) * g
+        v *= b2
+        v += (1 - b2) * g * g
+        p -= lr * (m / (1 - b1 ** t)) / (np.sqrt(v / (1 - b2 ** t)) + eps)
+
+
+def _flat(p, prefix=""):
+    out = {}
+    for k, v in p.items():
+        if isinstance(v, list):
+            for i, d in enumerate(v):
+                out.update(_flat(d, f"{prefix}{k}{i}."))
+        else:
+            out[prefix + k] = v
+    return out
+
+
+def cpu_reference_steps(widened, sample_images, steps, warmup, min_seconds=0.0):
+    """Runs the training step with the reference's host-compiled kernels;
+    returns (images/s, cores, kind, seconds, steps_done)."""
+    import torch
+    from oracle.netstep import params_of, train_grads
+    from oracle.oracle import Oracle, available
+    from opencl_tf.model import build_model
+    kind = "reference" if available("ref") else "port"
+    o = Oracle("ref" if kind == "reference" else "port")
+    torch.manual_seed(0)
+    model = build_model(widened=widened)
+    p = params_of(model)
+    w = workload(widened)
+    x, t = make_batch(sample_images, w["in_hw"], w["out_hw"], 1234)
+    head = (8, 8, 8) if widened else (4, 4, 8)
+    flat = _flat(p)
+    state = {}
+
+    def step():
+        _, _, g = train_grads(o, p, x, t, head=head)
+        adam_np(flat, _flat(g), state)
+
+    for _ in range(warmup):
+        step()
+    done, t0 = 0, time.perf_counter()
+    while done < steps or (time.perf_counter() - t0) < min_seconds:
+        step()
+        done += 1
+    dt = time.perf_counter() - t0
+    return sample_images * done / dt, o.threads(), kind, dt, done
+
+
+# ------------------------------------------------------------------ ours
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import opencl_tf
+    from opencl_tf import profile
+    from opencl_tf.model import build_model
+    from opencl_tf.train import TrainStep
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = workload(args.widened)
+    B = w["batch_per_gpu"]
+    torch.manual_seed(0)
+    model = build_model(widened=args.widened, device=dev)
+    x_np, t_np = make_batch(B, w["in_hw"], w["out_hw"], 1000 + rank)
+    x_dev = torch.from_numpy(x_np).to(dev)
+    t_dev = torch.from_numpy(t_np).to(dev)
+    step = TrainStep(model, lr=1e-3, graphed=True, warmup=3)
+    flush = profile._Flusher(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- warm-up (the first call also captures the graph)
+    launches0 = opencl_tf._library.kernel_launch_count()
+    step(x_dev, t_dev)
+    launches_capture = opencl_tf._library.kernel_launch_count() - launches0
+    for _ in range(max(args.warmup - 1, 0)):
+        step(x_dev, t_dev)
+    # kernels per step: the captured step enqueued launches_capture / 4 of ours (3 eager warm-ups + capture)
+    per_step_launches = launches_capture // 4
+
+    uuids = []
+    try:
+        uuids = [str(torch.cuda.get_device_properties(dev).uuid)]
+    except Exception:  # noqa: BLE001
+        pass
+    clocks = ClockSampler(uuids)
+
+    def timed(fn, K):
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+        barrier()
+        for i in range(K):
+            flush()
+            starts[i].record()
+            fn()
+            ends[i].record()
+        barrier()
+        ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        if world > 1:
+            tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms
+
+    clocks.start()
+    time.sleep(0.3)
+    ms_dev = timed(lambda: step(x_dev, t_dev), args.steps)
+
+    # ---- end to end: pinned host batch in, loss out, every step
+    x_host = torch.from_numpy(x_np).pin_memory()
+    t_host = torch.from_numpy(t_np).pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        step.static_x.copy_(x_host, non_blocking=True)
+        step.static_y.copy_(t_host, non_blocking=True)
+        loss = step(step.static_x, step.static_y)
+        loss_host.copy_(loss, non_blocking=True)
+
+    ms_e2e = timed(e2e_step, args.steps)
+    clk = clocks.stop()
+    loss_value = float(loss_host)
+
+    # ---- per-op table and the dominant op's roofline (rank 0, outside the timed regions)
+    per_op, roof = None, None
+    if rank == 0:
+        from opencl_tf.train import mse
+        _, log = profile.record_step(lambda: mse(model(x_dev, training=True), t_dev).backward())
+        rows = profile.time_ops(log, reps=5, device=dev)
+        per_op = profile.summarize(rows)
+        top = max(rows, key=lambda r: r["ms"])
+        roof = {"kernel": top["op"], "bound": top["bound"], "achieved": round(top["achieved"], 1),
+                "peak": round(top["peak"], 1), "unit": top["unit"], "frac": round(top["frac"], 4),
+                "peak_source": profile.peaks()["source"], "traffic": None,
+                "algorithmic_bytes": top["bytes"], "algorithmic_flops": top["flops"], "ms": round(top["ms"], 4),
+                "step_ms_sum_of_ops": round(sum(r["ms"] for r in rows), 4)}
+        model.zero_grad(set_to_none=True)
+
+    # ---- CPU baseline (rank 0 at N=1 only; bounded sample)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, 16 if not args.widened else 1, 1, 1,
+                                                             min_seconds=10.0)
+        cpu = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": kind,
+               "sample": f"{nsteps} training steps of {16 if not args.widened else 1} images (of the {B}-image "
+                         f"batch) through the host-compiled reference kernels, {secs:.1f} s"}
+
+    images = B * world * args.steps
+    line = {
+        "metric": METRIC, "value": round(images / (ms_dev * 1e-3), 2), "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w["workload"], "global_batch": B * world, "per_gpu_batch": B,
+                   "parallelism": f"dp{world}", "cuda_graph": True,
+                   "l2": "flushed between timed steps (256 MiB write outside the step's events)",
+                   "math": "fp32 activations; contractions on tcgen05 tensor cores in 3xTF32"},
+        "e2e": {"value": round(images / (ms_e2e * 1e-3), 2), "unit": "images/s",
+                "h2d_bytes_per_step": int(x_host.numel() * 4 + t_host.numel() * 4), "d2h_bytes_per_step": 4,
+                "ms_per_step": round(ms_e2e / args.steps, 4)},
+        "gpu_launches": int(per_step_launches * args.steps),
+        "roofline": roof, "per_op": per_op, "cpu_baseline": cpu, "clocks": clk,
+        "final_loss": round(loss_value, 6),
+        "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
+    }
+    step.release()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--widened", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    w = workload(args.widened)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        sample = 16 if not args.widened else 1
+        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, sample, args.steps, args.warmup)
+        line = {"metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / nsteps * 1e3, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "impl": "reference",
+                "config": {"workload": w["workload"], "global_batch": w["batch_per_gpu"] * args.gpus,
+                           "per_gpu_batch": w["batch_per_gpu"], "parallelism": f"dp{args.gpus}"},
+                "cpu_baseline": {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": kind,
+                                 "sample": f"each step is {sample} images of the batch through the reference's "
+                                           f"kernels compiled for the host (OpenMP over work-items)"},
+                "e2e": {"value": round(ips, 3), "unit": "images/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,429 @@
+// batchnorm.cu -- BatchNorm training forward, inference forward, gradient.
+//
+// Reference: kernels/batchnorm_kernels.cl and src/ops/batchnorm_ops.cc.  The
+// reference reduces with ONE work-item per channel walking all N*H*W rows
+// (batchnorm_kernels.cl:35-60, 84-116).  Here each reduction is two
+// deterministic stages:
+//
+//   partial:  a grid of (row block x channel chunk) CTAs; threads own a
+//             channel group (4 channels with float4 loads when C % 4 == 0)
+//             and stride over the rows of their block, then the CTA folds
+//             its rows in a fixed order and writes one partial per channel;
+//   finalize: one warp per channel sums the partials (lane-strided, then a
+//             shuffle tree) and derives the per-channel outputs and the
+//             per-channel constants of the elementwise pass.
+//
+// The block count depends only on the shape and the SM count, so results
+// are bit-reproducible run to run.  The elementwise passes evaluate the
+// reference formulas with round-to-nearest intrinsics (no contraction) and
+// inv_std = 1/sqrt(var+eps) in IEEE fp32, so, given the same statistics,
+// y and grad_x are bit-identical to the reference's formula.
+#include "b2_internal.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct ChunkGeom {
+  int vec;       // 4 when C % 4 == 0 and pointers are 16-byte aligned, else 1
+  int groups;    // channel groups of `vec` channels = C / vec
+  int cg;        // channel groups per CTA (<= kThreads)
+  int chunks;    // CTAs along the channel axis
+  int rpi;       // rows a CTA advances per iteration = kThreads / cg
+};
+
+ChunkGeom chunk_geom(int64_t C, bool vec_ok) {
+  ChunkGeom g;
+  g.vec = vec_ok ? 4 : 1;
+  g.groups = (int)(C / g.vec);
+  g.cg = g.groups < kThreads ? g.groups : kThreads;
+  g.chunks = (int)ceil_div(g.groups, g.cg);
+  g.rpi = kThreads / g.cg;
+  return g;
+}
+
+// Row blocks for the partial stage: about 4 CTAs per SM in total, at least
+// 32 rows per CTA.
+int row_blocks(int64_t rows, int chunks, int sm_count) {
+  int64_t want = (int64_t)sm_count * 4 / chunks;
+  if (want < 1) want = 1;
+  int64_t cap = ceil_div(rows, 32);
+  if (cap < 1) cap = 1;
+  return (int)(want < cap ? want : cap);
+}
+
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<1> {
+  using T = float;
+  __device__ static void to(const T& v, float* o) { o[0] = v; }
+};
+template <>
+struct VecT<4> {
+  using T = float4;
+  __device__ static void to(const T& v, float* o) {
+    o[0] = v.x;
+    o[1] = v.y;
+    o[2] = v.z;
+    o[3] = v.w;
+  }
+};
+
+// Stage 1.  MODE 0: (sum x, sum x^2).  MODE 1: (sum dy, sum dy * x_hat) with
+// x_hat = (x - mean) * inv_std, inv_std = 1/sqrt(var + eps) per channel.
+template <int VEC, int MODE>
+__global__ void __launch_bounds__(kThreads)
+    bn_partial_kernel(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ mean,
+                      const float* __restrict__ var, float eps, int64_t rows, int C, ChunkGeom geo,
+                      float2* __restrict__ partial) {
+  using V = typename VecT<VEC>::T;
+  __shared__ float s_a[kThreads * VEC];
+  __shared__ float s_b[kThreads * VEC];
+  __shared__ float s_mean[kThreads * VEC];
+  __shared__ float s_inv[kThreads * VEC];
+
+  const int chunk = blockIdx.y;
+  const int t = threadIdx.x;
+  const int cg_local = t % geo.cg;
+  const int r_off = t / geo.cg;
+  const int group = chunk * geo.cg + cg_local;
+  const bool active = r_off < geo.rpi && group < geo.groups;
+  const int c0 = group * VEC;
+
+  if (MODE == 1) {
+    for (int i = t; i < geo.cg * VEC; i += kThreads) {
+      const int c = chunk * geo.cg * VEC + i;
+      if (c < C) {
+        s_mean[i] = mean[c];
+        s_inv[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[c], eps)));
+      }
+    }
+    __syncthreads();
+  }
+
+  const int64_t per_block = ceil_div(rows, gridDim.x);
+  const int64_t r_begin = (int64_t)blockIdx.x * per_block;
+  int64_t r_end = r_begin + per_block;
+  if (r_end > rows) r_end = rows;
+
+  float acc_a[VEC], acc_b[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) acc_a[j] = acc_b[j] = 0.0f;
+
+  if (active) {
+    const int loc = cg_local * VEC;
+    for (int64_t r = r_begin + r_off; r < r_end; r += geo.rpi) {
+      float v[VEC];
+      VecT<VEC>::to(*reinterpret_cast<const V*>(x + r * C + c0), v);
+      if (MODE == 0) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          acc_a[j] += v[j];
+          acc_b[j] = fmaf(v[j], v[j], acc_b[j]);
+        }
+      } else {
+        float g[VEC];
+        VecT<VEC>::to(*reinterpret_cast<const V*>(dy + r * C + c0), g);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xh = (v[j] - s_mean[loc + j]) * s_inv[loc + j];
+          acc_a[j] += g[j];
+          acc_b[j] = fmaf(g[j], xh, acc_b[j]);
+        }
+      }
+    }
+  }
+  // Fold the rpi row lanes of each channel in a fixed order.
+  if (r_off < geo.rpi) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      s_a[r_off * geo.cg * VEC + cg_local * VEC + j] = acc_a[j];
+      s_b[r_off * geo.cg * VEC + cg_local * VEC + j] = acc_b[j];
+    }
+  }
+  __syncthreads();
+  const int width = geo.cg * VEC;
+  for (int i = t; i < width; i += kThreads) {
+    const int c = chunk * width + i;
+    if (c >= C) continue;
+    float a = 0.0f, b = 0.0f;
+    for (int r = 0; r < geo.rpi; ++r) {
+      a += s_a[r * width + i];
+      b += s_b[r * width + i];
+    }
+    partial[(int64_t)blockIdx.x * C + c] = make_float2(a, b);
+  }
+}
+
+// Stage 2 for the statistics: saved_mean, saved_var (biased, E[x^2]-mean^2 as
+// batchnorm_kernels.cl:57-59) and the constants of the normalize pass.
+__global__ void bn_stats_finalize_kernel(const float2* __restrict__ partial, int blocks, int C, int64_t nhw,
+                                         float eps, float* __restrict__ mean, float* __restrict__ var,
+                                         float* __restrict__ inv_std) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= C) return;
+  float a = 0.0f, b = 0.0f;
+  for (int i = lane; i < blocks; i += 32) {
+    const float2 p = partial[(int64_t)i * C + warp];
+    a += p.x;
+    b += p.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (lane == 0) {
+    const float n = (float)(int)nhw;  // the reference divides by (float)(int)NHW
+    const float m = __fdiv_rn(a, n);
+    const float v = __fsub_rn(__fdiv_rn(b, n), __fmul_rn(m, m));
+    mean[warp] = m;
+    var[warp] = v;
+    inv_std[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v, eps)));
+  }
+}
+
+// inv_std for the inference op (batchnorm_kernels.cl:78).
+__global__ void bn_inv_std_kernel(const float* __restrict__ var, int C, float eps, float* __restrict__ inv_std) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < C) inv_std[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[c], eps)));
+}
+
+// y = gamma * ((x - mean) * inv_std) + beta (batchnorm_kernels.cl:77-80).
+template <int VEC>
+__global__ void __launch_bounds__(kThreads)
+    bn_normalize_kernel(const float* __restrict__ x, const float* __restrict__ mean,
+                        const float* __restrict__ inv_std, const float* __restrict__ gamma,
+                        const float* __restrict__ beta, float* __restrict__ y, int64_t total, int C) {
+  using V = typename VecT<VEC>::T;
+  const int64_t nv = total / VEC;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  int c0 = (int)((i * VEC) % C);
+  const int step = (int)((stride * VEC) % C);
+  for (; i < nv; i += stride, c0 = (c0 + step >= C) ? c0 + step - C : c0 + step) {
+    float v[VEC], o[VEC];
+    VecT<VEC>::to(reinterpret_cast<const V*>(x)[i], v);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int c = c0 + j;
+      const float xh = __fmul_rn(__fsub_rn(v[j], __ldg(mean + c)), __ldg(inv_std + c));
+      o[j] = __fadd_rn(__fmul_rn(__ldg(gamma + c), xh), __ldg(beta + c));
+    }
+    if (VEC == 4)
+      reinterpret_cast<float4*>(y)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    else
+      y[i] = o[0];
+  }
+}
+
+// Stage 2 of the gradient: grad_beta = sum dy, grad_gamma = sum dy * x_hat;
+// also k1 = gamma * inv_std / NHW and inv_std for the dx pass.
+__global__ void bn_grad_finalize_kernel(const float2* __restrict__ partial, int blocks, int C, int64_t nhw,
+                                        float eps, const float* __restrict__ gamma, const float* __restrict__ var,
+                                        float* __restrict__ grad_beta, float* __restrict__ grad_gamma,
+                                        float* __restrict__ k1, float* __restrict__ inv_std) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= C) return;
+  float a = 0.0f, b = 0.0f;
+  for (int i = lane; i < blocks; i += 32) {
+    const float2 p = partial[(int64_t)i * C + warp];
+    a += p.x;
+    b += p.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (lane == 0) {
+    grad_beta[warp] = a;
+    grad_gamma[warp] = b;
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[warp], eps)));
+    const float n = (float)(int)nhw;
+    inv_std[warp] = inv;
+    k1[warp] = __fdiv_rn(__fmul_rn(gamma[warp], inv), n);
+  }
+}
+
+// dx = k1 * (NHW*dy - grad_beta - x_hat*grad_gamma) (batchnorm_kernels.cl:135-142)
+template <int VEC>
+__global__ void __launch_bounds__(kThreads)
+    bn_grad_dx_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
+                      const float* __restrict__ inv_std, const float* __restrict__ k1,
+                      const float* __restrict__ grad_beta, const float* __restrict__ grad_gamma,
+                      float* __restrict__ dx, int64_t total, int C, float nhw_f) {
+  using V = typename VecT<VEC>::T;
+  const int64_t nv = total / VEC;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  int c0 = (int)((i * VEC) % C);
+  const int step = (int)((stride * VEC) % C);
+  for (; i < nv; i += stride, c0 = (c0 + step >= C) ? c0 + step - C : c0 + step) {
+    float vx[VEC], vg[VEC], o[VEC];
+    VecT<VEC>::to(reinterpret_cast<const V*>(x)[i], vx);
+    VecT<VEC>::to(reinterpret_cast<const V*>(dy)[i], vg);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int c = c0 + j;
+      const float xh = __fmul_rn(__fsub_rn(vx[j], __ldg(mean + c)), __ldg(inv_std + c));
+      float t = __fmul_rn(nhw_f, vg[j]);
+      t = __fsub_rn(t, __ldg(grad_beta + c));
+      t = __fsub_rn(t, __fmul_rn(xh, __ldg(grad_gamma + c)));
+      o[j] = __fmul_rn(__ldg(k1 + c), t);
+    }
+    if (VEC == 4)
+      reinterpret_cast<float4*>(dx)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    else
+      dx[i] = o[0];
+  }
+}
+
+int validate_nhwc(const int64_t* s, const char* what) {
+  B2_REQUIRE(s != nullptr, "%s shape missing", what);
+  for (int i = 0; i < 4; ++i) B2_REQUIRE(s[i] >= 0, "%s must be NHWC with non-negative dims", what);
+  B2_REQUIRE(s[0] * s[1] * s[2] * s[3] <= kMaxInt32 * 4, "%s is too large", what);
+  return B2_OK;
+}
+
+int launch_partials(cudaStream_t s, int mode, const float* x, const float* dy, const float* mean,
+                    const float* var, float eps, int64_t rows, int C, bool vec_ok, const DeviceInfo* d,
+                    float2* partial, int* blocks_out) {
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  dim3 grid(blocks, geo.chunks);
+  if (geo.vec == 4) {
+    if (mode == 0)
+      bn_partial_kernel<4, 0><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+    else
+      bn_partial_kernel<4, 1><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+  } else {
+    if (mode == 0)
+      bn_partial_kernel<1, 0><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+    else
+      bn_partial_kernel<1, 1><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+  }
+  *blocks_out = blocks;
+  return check_launch(s, mode == 0 ? "bn_reduce_stats" : "bn_backward_reduce");
+}
+
+int launch_normalize(cudaStream_t s, const float* x, const float* mean, const float* inv, const float* gamma,
+                     const float* beta, float* y, int64_t total, int C, bool vec_ok) {
+  if (vec_ok) {
+    bn_normalize_kernel<4><<<grid_for(total / 4, kThreads, 8), kThreads, 0, s>>>(x, mean, inv, gamma, beta, y,
+                                                                               total, C);
+  } else {
+    bn_normalize_kernel<1><<<grid_for(total, kThreads, 8), kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, total,
+                                                                           C);
+  }
+  return check_launch(s, "bn_normalize");
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+// src/ops/batchnorm_ops.cc:87-180
+int b2_batch_norm_training(b2_stream_t stream, const float* x, const int64_t x_shape[4], const float* gamma,
+                           int64_t gamma_len, const float* beta, int64_t beta_len, float epsilon, float* y,
+                           float* saved_mean, float* saved_var) {
+  clear_error();
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  const int64_t C = x_shape[3];
+  B2_REQUIRE(gamma_len == C && beta_len == C, "gamma/beta size must equal channels");
+  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
+  const int64_t total = rows * C;
+  if (C == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  Scratch part, inv;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
+  B2_RETURN_IF_ERROR(inv.alloc(sizeof(float) * C, s));
+  int used_blocks = 0;
+  B2_RETURN_IF_ERROR(launch_partials(s, 0, x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, vec_ok, d,
+                                     part.as<float2>(), &used_blocks));
+  bn_stats_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+                                                                       epsilon, saved_mean, saved_var,
+                                                                       inv.as<float>());
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
+  if (total == 0) return B2_OK;
+  return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok);
+}
+
+// src/ops/batchnorm_ops.cc:213-275
+int b2_batch_norm_inference(b2_stream_t stream, const float* x, const int64_t x_shape[4], const float* gamma,
+                            int64_t gamma_len, const float* beta, int64_t beta_len, const float* mean,
+                            int64_t mean_len, const float* var, int64_t var_len, float epsilon, float* y) {
+  clear_error();
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  const int64_t C = x_shape[3];
+  B2_REQUIRE(gamma_len == C && beta_len == C && mean_len == C && var_len == C,
+             "gamma/beta/mean/var must have C elements");
+  const int64_t total = x_shape[0] * x_shape[1] * x_shape[2] * C;
+  if (total == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Scratch inv;
+  B2_RETURN_IF_ERROR(inv.alloc(sizeof(float) * C, s));
+  bn_inv_std_kernel<<<(int)ceil_div(C, 256), 256, 0, s>>>(var, (int)C, epsilon, inv.as<float>());
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_inv_std"));
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
+  return launch_normalize(s, x, mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok);
+}
+
+// src/ops/batchnorm_ops.cc:313-416
+int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t grad_y_shape[4], const float* x,
+                       const int64_t x_shape[4], const float* gamma, const float* saved_mean,
+                       const float* saved_var, float epsilon, float* grad_x, float* grad_gamma, float* grad_beta) {
+  clear_error();
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  bool same_shape = grad_y_shape != nullptr;
+  for (int i = 0; same_shape && i < 4; ++i) same_shape = grad_y_shape[i] == x_shape[i];
+  B2_REQUIRE(same_shape, "grad_y and x must have matching NHWC shapes");
+  const int64_t C = x_shape[3];
+  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
+  const int64_t total = rows * C;
+  if (C == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(grad_y) && aligned16(grad_x);
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  Scratch part, chan;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
+  B2_RETURN_IF_ERROR(chan.alloc(sizeof(float) * 2 * C, s));
+  float* k1 = chan.as<float>();
+  float* inv = k1 + C;
+  int used_blocks = 0;
+  B2_RETURN_IF_ERROR(launch_partials(s, 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C, vec_ok, d,
+                                     part.as<float2>(), &used_blocks));
+  bn_grad_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+                                                                      epsilon, gamma, saved_var, grad_beta,
+                                                                      grad_gamma, k1, inv);
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
+  if (total == 0) return B2_OK;
+  const float nhw_f = (float)(int)rows;
+  if (vec_ok) {
+    bn_grad_dx_kernel<4><<<grid_for(total / 4, kThreads, 8), kThreads, 0, s>>>(
+        grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x, total, (int)C, nhw_f);
+  } else {
+    bn_grad_dx_kernel<1><<<grid_for(total, kThreads, 8), kThreads, 0, s>>>(
+        grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x, total, (int)C, nhw_f);
+  }
+  return check_launch(s, "bn_backward_dx");
+}
+
+}  // extern "C"

@@ -1,0 +1,445 @@
+// depthwise.cu -- DepthwiseConv2D forward, input gradient, filter gradient.
+//
+// Reference: kernels/depthwise_conv2d_kernels.cl, src/ops/
+// depthwise_conv2d_ops.cc.  Output channel co = ci*dm + d sees only input
+// channel ci.  These ops are HBM-bound (about 2*kH*kW flops per output), so
+// the kernels are built around coalesced NHWC traffic:
+//
+//   forward / input gradient, dm == 1 and C % 4 == 0: one thread per
+//     (pixel, 4 channels) with 128-bit loads; taps summed in the reference's
+//     (kh, kw[, d]) order with round-to-nearest multiply and add, so every
+//     output is bit-identical to the reference's sequential fp32 sum;
+//   other shapes: one thread per element, same order, same exactness;
+//   filter gradient: a sum over N*Ho*Wo per filter element, done as per-CTA
+//     partial sums (each thread owns 4 channels x all taps, CTAs fold their
+//     pixel lanes in a fixed order) plus a fixed-order finalize, so it is
+//     deterministic; with dm > 1 or C % 4 != 0 a scalar variant of the same
+//     two stages.
+#include "conv_common.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float4 fadd4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 fmul4(float4 a, float4 b) {
+  return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+
+struct DwArgs {
+  int N, H, W, C, kH, kW, dm, sH, sW, pH, pW, Ho, Wo;
+};
+
+DwArgs to_args(const ConvGeom& g) {
+  DwArgs a;
+  a.N = (int)g.N; a.H = (int)g.H; a.W = (int)g.W; a.C = (int)g.Ci;
+  a.kH = (int)g.kH; a.kW = (int)g.kW; a.dm = (int)g.dm;
+  a.sH = (int)g.sH; a.sW = (int)g.sW; a.pH = (int)g.pH; a.pW = (int)g.pW;
+  a.Ho = (int)g.Ho; a.Wo = (int)g.Wo;
+  return a;
+}
+
+// --------------------------------------------------------------- forward
+
+// depthwise_conv2d_kernels.cl:16-56, dm == 1, 4 channels per thread.
+__global__ void __launch_bounds__(kThreads) dw_fwd_vec4_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ w, float* __restrict__ y,
+                                                                DwArgs a) {
+  const int cg = a.C >> 2;
+  const int64_t total = (int64_t)a.N * a.Ho * a.Wo * cg;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
+    const int c = (int)(g % cg) * 4;
+    int64_t p = g / cg;
+    const int wo = (int)(p % a.Wo);
+    p /= a.Wo;
+    const int ho = (int)(p % a.Ho);
+    const int n = (int)(p / a.Ho);
+    const int hi0 = ho * a.sH - a.pH, wi0 = wo * a.sW - a.pW;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int kh = 0; kh < a.kH; ++kh) {
+      const int hi = hi0 + kh;
+      if ((unsigned)hi >= (unsigned)a.H) continue;
+      const float* xrow = x + ((int64_t)(n * a.H + hi) * a.W) * a.C + c;
+      const float* wrow = w + (int64_t)(kh * a.kW) * a.C + c;
+      for (int kw = 0; kw < a.kW; ++kw) {
+        const int wi = wi0 + kw;
+        if ((unsigned)wi >= (unsigned)a.W) continue;
+        const float4 xv = __ldg(reinterpret_cast<const float4*>(xrow + (int64_t)wi * a.C));
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + (int64_t)kw * a.C));
+        acc = fadd4(acc, fmul4(xv, wv));
+      }
+    }
+    reinterpret_cast<float4*>(y)[g] = acc;
+  }
+}
+
+// depthwise_conv2d_kernels.cl:16-56, any dm / C.
+__global__ void __launch_bounds__(kThreads) dw_fwd_scalar_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ w,
+                                                                  float* __restrict__ y, DwArgs a) {
+  const int Co = a.C * a.dm;
+  const int64_t total = (int64_t)a.N * a.Ho * a.Wo * Co;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
+    const int co = (int)(g % Co);
+    int64_t p = g / Co;
+    const int wo = (int)(p % a.Wo);
+    p /= a.Wo;
+    const int ho = (int)(p % a.Ho);
+    const int n = (int)(p / a.Ho);
+    const int ci = co / a.dm, d = co % a.dm;
+    float acc = 0.0f;
+    for (int kh = 0; kh < a.kH; ++kh) {
+      const int hi = ho * a.sH - a.pH + kh;
+      if ((unsigned)hi >= (unsigned)a.H) continue;
+      for (int kw = 0; kw < a.kW; ++kw) {
+        const int wi = wo * a.sW - a.pW + kw;
+        if ((unsigned)wi >= (unsigned)a.W) continue;
+        acc = __fadd_rn(acc, __fmul_rn(__ldg(x + ((int64_t)(n * a.H + hi) * a.W + wi) * a.C + ci),
+                                       __ldg(w + ((int64_t)(kh * a.kW + kw) * a.C + ci) * a.dm + d)));
+      }
+    }
+    y[g] = acc;
+  }
+}
+
+// ----------------------------------------------------------- input grad
+
+// depthwise_conv2d_kernels.cl:59-104, dm == 1, 4 channels per thread.
+__global__ void __launch_bounds__(kThreads) dw_dgrad_vec4_kernel(const float* __restrict__ dy,
+                                                                  const float* __restrict__ w,
+                                                                  float* __restrict__ dx, DwArgs a) {
+  const int cg = a.C >> 2;
+  const int64_t total = (int64_t)a.N * a.H * a.W * cg;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
+    const int c = (int)(g % cg) * 4;
+    int64_t p = g / cg;
+    const int wi = (int)(p % a.W);
+    p /= a.W;
+    const int hi = (int)(p % a.H);
+    const int n = (int)(p / a.H);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int kh = 0; kh < a.kH; ++kh) {
+      const int hn = hi + a.pH - kh;
+      if (hn < 0 || hn % a.sH != 0) continue;
+      const int ho = hn / a.sH;
+      if (ho >= a.Ho) continue;
+      for (int kw = 0; kw < a.kW; ++kw) {
+        const int wn = wi + a.pW - kw;
+        if (wn < 0 || wn % a.sW != 0) continue;
+        const int wo = wn / a.sW;
+        if (wo >= a.Wo) continue;
+        const float4 gv =
+            __ldg(reinterpret_cast<const float4*>(dy + ((int64_t)(n * a.Ho + ho) * a.Wo + wo) * a.C + c));
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)(kh * a.kW + kw) * a.C + c));
+        acc = fadd4(acc, fmul4(gv, wv));
+      }
+    }
+    reinterpret_cast<float4*>(dx)[g] = acc;
+  }
+}
+
+// depthwise_conv2d_kernels.cl:59-104, any dm / C.
+__global__ void __launch_bounds__(kThreads) dw_dgrad_scalar_kernel(const float* __restrict__ dy,
+                                                                    const float* __restrict__ w,
+                                                                    float* __restrict__ dx, DwArgs a) {
+  const int Co = a.C * a.dm;
+  const int64_t total = (int64_t)a.N * a.H * a.W * a.C;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
+    const int ci = (int)(g % a.C);
+    int64_t p = g / a.C;
+    const int wi = (int)(p % a.W);
+    p /= a.W;
+    const int hi = (int)(p % a.H);
+    const int n = (int)(p / a.H);
+    float acc = 0.0f;
+    for (int kh = 0; kh < a.kH; ++kh) {
+      const int hn = hi + a.pH - kh;
+      if (hn < 0 || hn % a.sH != 0) continue;
+      const int ho = hn / a.sH;
+      if (ho >= a.Ho) continue;
+      for (int kw = 0; kw < a.kW; ++kw) {
+        const int wn = wi + a.pW - kw;
+        if (wn < 0 || wn % a.sW != 0) continue;
+        const int wo = wn / a.sW;
+        if (wo >= a.Wo) continue;
+        const float* gp = dy + ((int64_t)(n * a.Ho + ho) * a.Wo + wo) * Co + (int64_t)ci * a.dm;
+        const float* wp = w + ((int64_t)(kh * a.kW + kw) * a.C + ci) * a.dm;
+        for (int d = 0; d < a.dm; ++d) acc = __fadd_rn(acc, __fmul_rn(__ldg(gp + d), __ldg(wp + d)));
+      }
+    }
+    dx[g] = acc;
+  }
+}
+
+// ---------------------------------------------------------- filter grad
+
+// Stage 1, dm == 1, C % 4 == 0, kH*kW <= KMAX: thread (channel group, pixel
+// lane) accumulates all taps for 4 channels over its pixels; the CTA folds
+// its pixel lanes per tap in a fixed order.  partial: [blocks][kH*kW*C].
+template <int KMAX>
+__global__ void __launch_bounds__(kThreads) dw_wgrad_partial_vec4_kernel(const float* __restrict__ x,
+                                                                          const float* __restrict__ dy,
+                                                                          float* __restrict__ partial, DwArgs a,
+                                                                          int cg_per_cta, int64_t pix_per_block) {
+  __shared__ float4 s_fold[kThreads];
+  const int cg_total = a.C >> 2;
+  const int lanes = kThreads / cg_per_cta;
+  const int t = threadIdx.x;
+  const int cgl = t % cg_per_cta;
+  const int lane = t / cg_per_cta;
+  const int cgi = blockIdx.y * cg_per_cta + cgl;
+  const bool active = lane < lanes && cgi < cg_total;
+  const int c = cgi * 4;
+  const int taps = a.kH * a.kW;
+  const int64_t pixels = (int64_t)a.N * a.Ho * a.Wo;
+  const int64_t p_begin = (int64_t)blockIdx.x * pix_per_block;
+  int64_t p_end = p_begin + pix_per_block;
+  if (p_end > pixels) p_end = pixels;
+
+  float4 acc[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  if (active) {
+    for (int64_t p = p_begin + lane; p < p_end; p += lanes) {
+      const int wo = (int)(p % a.Wo);
+      const int64_t q = p / a.Wo;
+      const int ho = (int)(q % a.Ho);
+      const int n = (int)(q / a.Ho);
+      const float4 gv = __ldg(reinterpret_cast<const float4*>(dy + p * a.C + c));
+      const int hi0 = ho * a.sH - a.pH, wi0 = wo * a.sW - a.pW;
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        if (k < taps) {
+          const int hi = hi0 + k / a.kW, wi = wi0 + k % a.kW;
+          if ((unsigned)hi < (unsigned)a.H && (unsigned)wi < (unsigned)a.W) {
+            const float4 xv =
+                __ldg(reinterpret_cast<const float4*>(x + ((int64_t)(n * a.H + hi) * a.W + wi) * a.C + c));
+            acc[k].x = fmaf(xv.x, gv.x, acc[k].x);
+            acc[k].y = fmaf(xv.y, gv.y, acc[k].y);
+            acc[k].z = fmaf(xv.z, gv.z, acc[k].z);
+            acc[k].w = fmaf(xv.w, gv.w, acc[k].w);
+          }
+        }
+      }
+    }
+  }
+  const int64_t out_base = (int64_t)blockIdx.x * taps * a.C;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    if (k >= taps) break;
+    __syncthreads();
+    s_fold[t] = acc[k];
+    __syncthreads();
+    if (lane == 0 && cgi < cg_total) {
+      float4 s = s_fold[cgl];
+      for (int l = 1; l < lanes; ++l) {
+        const float4 v = s_fold[l * cg_per_cta + cgl];
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      *reinterpret_cast<float4*>(partial + out_base + (int64_t)k * a.C + c) = s;
+    }
+  }
+}
+
+// Stage 1, any shape: one CTA per (pixel chunk, filter-element chunk); each
+// thread owns one filter element and walks the chunk's pixels.
+__global__ void __launch_bounds__(kThreads) dw_wgrad_partial_scalar_kernel(const float* __restrict__ x,
+                                                                            const float* __restrict__ dy,
+                                                                            float* __restrict__ partial, DwArgs a,
+                                                                            int64_t pix_per_block) {
+  const int F = a.kH * a.kW * a.C * a.dm;
+  const int f = blockIdx.y * kThreads + threadIdx.x;
+  if (f >= F) return;
+  const int d = f % a.dm;
+  const int ci = (f / a.dm) % a.C;
+  const int kw = (f / (a.dm * a.C)) % a.kW;
+  const int kh = f / (a.dm * a.C * a.kW);
+  const int Co = a.C * a.dm;
+  const int co = ci * a.dm + d;
+  const int64_t pixels = (int64_t)a.N * a.Ho * a.Wo;
+  const int64_t p_begin = (int64_t)blockIdx.x * pix_per_block;
+  int64_t p_end = p_begin + pix_per_block;
+  if (p_end > pixels) p_end = pixels;
+  float acc = 0.0f;
+  for (int64_t p = p_begin; p < p_end; ++p) {
+    const int wo = (int)(p % a.Wo);
+    const int64_t q = p / a.Wo;
+    const int ho = (int)(q % a.Ho);
+    const int n = (int)(q / a.Ho);
+    const int hi = ho * a.sH - a.pH + kh, wi = wo * a.sW - a.pW + kw;
+    if ((unsigned)hi >= (unsigned)a.H || (unsigned)wi >= (unsigned)a.W) continue;
+    acc = fmaf(__ldg(x + ((int64_t)(n * a.H + hi) * a.W + wi) * a.C + ci), __ldg(dy + p * Co + co), acc);
+  }
+  partial[(int64_t)blockIdx.x * F + f] = acc;
+}
+
+// Stage 2: dw[f] = sum over blocks of partial[b][f], in block order.
+__global__ void dw_wgrad_finalize_kernel(const float* __restrict__ partial, int blocks, int F,
+                                         float* __restrict__ dw) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  float s = 0.0f;
+  for (int b = 0; b < blocks; ++b) s += partial[(int64_t)b * F + f];
+  dw[f] = s;
+}
+
+int dw_forward_geom(const int64_t* input_shape, const int64_t* filter_shape, const int32_t* strides,
+                    int num_strides, const char* padding, bool forward, ConvGeom* g) {
+  B2_RETURN_IF_ERROR(check_dims_nonneg(input_shape, 4, "input"));
+  B2_RETURN_IF_ERROR(check_dims_nonneg(filter_shape, 4, "filter"));
+  B2_RETURN_IF_ERROR(parse_conv_attrs(strides, num_strides, padding, forward, g));
+  g->N = input_shape[0]; g->H = input_shape[1]; g->W = input_shape[2]; g->Ci = input_shape[3];
+  g->kH = filter_shape[0]; g->kW = filter_shape[1]; g->dm = filter_shape[3];
+  g->Co = g->Ci * g->dm;
+  finish_geom(g);
+  return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+int b2_depthwise_conv2d_output_shape(const int64_t input_shape[4], const int64_t filter_shape[4],
+                                     const int32_t* strides, int num_strides, const char* padding,
+                                     int64_t out_shape[4]) {
+  clear_error();
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(dw_forward_geom(input_shape, filter_shape, strides, num_strides, padding, true, &g));
+  B2_REQUIRE(filter_shape[2] == input_shape[3], "filter[2] must equal input channels");
+  out_shape[0] = g.N; out_shape[1] = g.Ho; out_shape[2] = g.Wo; out_shape[3] = g.Co;
+  return B2_OK;
+}
+
+// src/ops/depthwise_conv2d_ops.cc:107-187
+int b2_depthwise_conv2d(b2_stream_t stream, const float* input, const int64_t input_shape[4], const float* filter,
+                        const int64_t filter_shape[4], const int32_t* strides, int num_strides, const char* padding,
+                        float* output, const int64_t output_shape[4]) {
+  clear_error();
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(dw_forward_geom(input_shape, filter_shape, strides, num_strides, padding, true, &g));
+  B2_REQUIRE(filter_shape[2] == g.Ci, "filter[2] must equal input channels");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(output_shape, 4, "output"));
+  B2_REQUIRE(output_shape[0] == g.N && output_shape[1] == g.Ho && output_shape[2] == g.Wo &&
+                 output_shape[3] == g.Co,
+             "output shape must be [N, Hout, Wout, C*depth_multiplier] = [%lld, %lld, %lld, %lld]",
+             (long long)g.N, (long long)g.Ho, (long long)g.Wo, (long long)g.Co);
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  if (g.out_elems() == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const DwArgs a = to_args(g);
+  if (g.dm == 1 && g.Ci % 4 == 0 && aligned16(input) && aligned16(filter) && aligned16(output)) {
+    dw_fwd_vec4_kernel<<<grid_for(g.out_elems() / 4, kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
+  } else {
+    dw_fwd_scalar_kernel<<<grid_for(g.out_elems(), kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
+  }
+  return check_launch(s, "dwconv2d_forward");
+}
+
+// src/ops/depthwise_conv2d_ops.cc:221-305
+int b2_depthwise_conv2d_backprop_input(b2_stream_t stream, const int32_t input_sizes[4], const float* filter,
+                                       const int64_t filter_shape[4], const float* out_backprop,
+                                       const int64_t out_backprop_shape[4], const int32_t* strides,
+                                       int num_strides, const char* padding, float* output) {
+  clear_error();
+  B2_REQUIRE(input_sizes != nullptr, "input_sizes must have 4 elements");
+  const int64_t in_shape[4] = {input_sizes[0], input_sizes[1], input_sizes[2], input_sizes[3]};
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(dw_forward_geom(in_shape, filter_shape, strides, num_strides, padding, false, &g));
+  B2_REQUIRE(filter_shape[2] == g.Ci, "filter[2] != C");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(out_backprop_shape, 4, "out_backprop"));
+  B2_REQUIRE(out_backprop_shape[0] == g.N && out_backprop_shape[1] == g.Ho && out_backprop_shape[2] == g.Wo &&
+                 out_backprop_shape[3] == g.Co,
+             "out_backprop shape mismatch");
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  if (g.in_elems() == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const DwArgs a = to_args(g);
+  if (g.dm == 1 && g.Ci % 4 == 0 && aligned16(out_backprop) && aligned16(filter) && aligned16(output)) {
+    dw_dgrad_vec4_kernel<<<grid_for(g.in_elems() / 4, kThreads, 8), kThreads, 0, s>>>(out_backprop, filter,
+                                                                                      output, a);
+  } else {
+    dw_dgrad_scalar_kernel<<<grid_for(g.in_elems(), kThreads, 8), kThreads, 0, s>>>(out_backprop, filter,
+                                                                                    output, a);
+  }
+  return check_launch(s, "dwconv2d_backprop_input");
+}
+
+// src/ops/depthwise_conv2d_ops.cc:341-426
+int b2_depthwise_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int64_t input_shape[4],
+                                        const int32_t filter_sizes[4], const float* out_backprop,
+                                        const int64_t out_backprop_shape[4], const int32_t* strides,
+                                        int num_strides, const char* padding, float* output) {
+  clear_error();
+  B2_REQUIRE(filter_sizes != nullptr, "filter_sizes must have 4 elements");
+  const int64_t f_shape[4] = {filter_sizes[0], filter_sizes[1], filter_sizes[2], filter_sizes[3]};
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(dw_forward_geom(input_shape, f_shape, strides, num_strides, padding, false, &g));
+  B2_REQUIRE(input_shape[3] == f_shape[2], "input channels != filter_sizes[2]");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(out_backprop_shape, 4, "out_backprop"));
+  B2_REQUIRE(out_backprop_shape[0] == g.N && out_backprop_shape[1] == g.Ho && out_backprop_shape[2] == g.Wo &&
+                 out_backprop_shape[3] == g.Co,
+             "out_backprop shape mismatch");
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  const int64_t F = g.kH * g.kW * g.Ci * g.dm;
+  if (F == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const DwArgs a = to_args(g);
+  const int64_t pixels = g.N * g.Ho * g.Wo;
+  if (pixels == 0) {
+    B2_CUDA_OR_RETURN(cudaMemsetAsync(output, 0, sizeof(float) * F, s));
+    return B2_OK;
+  }
+  const int taps = (int)(g.kH * g.kW);
+  const bool vec = g.dm == 1 && g.Ci % 4 == 0 && taps <= 9 && aligned16(input) && aligned16(out_backprop);
+  Scratch part;
+  int blocks = 0;
+  if (vec) {
+    const int cg_total = (int)(g.Ci / 4);
+    const int cg_per_cta = cg_total < kThreads ? cg_total : kThreads;
+    const int chunks = (int)ceil_div(cg_total, cg_per_cta);
+    int64_t want = (int64_t)d->sm_count * 4 / chunks;
+    if (want < 1) want = 1;
+    int64_t cap = ceil_div(pixels, 64);
+    blocks = (int)(want < cap ? want : cap);
+    const int64_t ppb = ceil_div(pixels, blocks);
+    blocks = (int)ceil_div(pixels, ppb);
+    B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * blocks * F, s));
+    dw_wgrad_partial_vec4_kernel<9><<<dim3(blocks, chunks), kThreads, 0, s>>>(input, out_backprop,
+                                                                              part.as<float>(), a, cg_per_cta, ppb);
+  } else {
+    int64_t want = (int64_t)d->sm_count * 2;
+    int64_t cap = ceil_div(pixels, 256);
+    blocks = (int)(want < cap ? want : cap);
+    if (blocks < 1) blocks = 1;
+    const int64_t ppb = ceil_div(pixels, blocks);
+    blocks = (int)ceil_div(pixels, ppb);
+    B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * blocks * F, s));
+    dw_wgrad_partial_scalar_kernel<<<dim3(blocks, (unsigned)ceil_div(F, kThreads)), kThreads, 0, s>>>(
+        input, out_backprop, part.as<float>(), a, ppb);
+  }
+  B2_RETURN_IF_ERROR(check_launch(s, "dwconv2d_backprop_filter"));
+  dw_wgrad_finalize_kernel<<<(int)ceil_div(F, 256), 256, 0, s>>>(part.as<float>(), blocks, (int)F, output);
+  return check_launch(s, "dwconv2d_backprop_filter_finalize");
+}
+
+}  // extern "C"

@@ -1,0 +1,513 @@
+// gemm_ops.cu -- Conv2D (forward, input grad, filter grad) and Dense
+// (forward, input grad, weight grad, bias grad) on the tcgen05 3xTF32 engine.
+//
+// Reference kernels: kernels/conv2d_kernels.cl:30-158 and
+// kernels/dense_kernels.cl:18-102 (one work-item per output, serial fp32
+// loops).  Each op is expressed as D[M,N] = A[M,K] . B[K,N] over views of the
+// caller's tensors, without materialising im2col or transposes:
+//
+//   op                     M            N      K              A view             B view
+//   conv2d forward         N*Ho*Wo      Co     kH*kW*Ci       im2col(x)          W[k,co]
+//   conv2d input grad      N*H*W        Ci     kH*kW*Co       strided gather dy  W[tap,ci,co]
+//   conv2d filter grad     kH*kW*Ci     Co     N*Ho*Wo        im2col(x)^T        dy[p,co]
+//   dense forward (+b)     batch        out_f  in_f           x                  W
+//   dense input grad       batch        in_f   out_f          dy                 W^T
+//   dense weight grad      in_f         out_f  batch          x^T                dy
+//
+// 1x1 / stride-1 / unpadded convolutions take the plain-matrix views.  When
+// the output tiles alone cannot fill the GPU (filter grads, the dense forward
+// at small batch) K is split across CTAs; partials are summed in split order
+// by a second kernel, so every result is deterministic.
+#include "conv_common.cuh"
+#include "tc_gemm.cuh"
+
+namespace b2 {
+namespace tc {
+
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N,
+                                     const float* __restrict__ bias, float* __restrict__ out, int64_t ldo) {
+  const int64_t total = M * N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    float s = 0.0f;
+    for (int z = 0; z < splits; ++z) s += part[(int64_t)z * total + i];
+    const int64_t m = i / N, n = i - m * N;
+    if (bias) s += bias[n];
+    out[m * ldo + n] = s;
+  }
+}
+
+int choose_bn(int64_t N) {
+  if (N <= 256) return (int)(ceil_div(N < 16 ? 16 : N, 16) * 16);
+  return N >= 2048 ? 256 : 128;
+}
+
+int choose_stages(int bn, int max_smem) {
+  const KernelSmem one = smem_plan(bn, 1);
+  int st = (int)((max_smem - (int)(one.total - one.stage_bytes)) / (int)one.stage_bytes);
+  if (st > kMaxStages) st = kMaxStages;
+  if (st < 2) st = 2;
+  return st;
+}
+
+int splits_for(int64_t tiles, int64_t K, int sm_count, int min_kb_per_split) {
+  if (tiles >= sm_count) return 1;
+  int64_t s = sm_count / tiles;
+  const int64_t cap = ceil_div(K, (int64_t)BK * min_kb_per_split);
+  if (s > cap) s = cap;
+  return s < 1 ? 1 : (int)s;
+}
+
+// ------------------------------------------------------- convolution views
+
+// A of the forward conv: row m = output pixel (n, ho, wo); k = (kh, kw, ci).
+struct ConvFpropA {
+  const float* x;
+  int64_t M;
+  int H, W, Ci, kW, sH, sW, pH, pW, Ho, Wo;
+  bool vec;  // Ci % 4 == 0 and x 16-byte aligned
+  struct Ctx {
+    const float* img;
+    int hi0, wi0;
+    bool valid;
+  };
+  __device__ Ctx row(int64_t m) const {
+    Ctx c;
+    c.valid = m < M;
+    if (!c.valid) m = 0;
+    const int wo = (int)(m % Wo);
+    const int64_t t = m / Wo;
+    const int ho = (int)(t % Ho);
+    const int64_t n = t / Ho;
+    c.img = x + n * H * W * Ci;
+    c.hi0 = ho * sH - pH;
+    c.wi0 = wo * sW - pW;
+    return c;
+  }
+  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+    if (!c.valid) {
+      zero_row(v);
+      return;
+    }
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < BK / 4; ++q) {
+        const int64_t k = k0 + 4 * q;
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < k_end) {
+          const int tap = (int)(k / Ci), ci = (int)(k - (int64_t)tap * Ci);
+          const int kh = tap / kW, kw = tap - kh * kW;
+          const int hi = c.hi0 + kh, wi = c.wi0 + kw;
+          if ((unsigned)hi < (unsigned)H && (unsigned)wi < (unsigned)W)
+            t = __ldg(reinterpret_cast<const float4*>(c.img + ((int64_t)hi * W + wi) * Ci + ci));
+        }
+        v[4 * q] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+      }
+    } else {
+      int tap = (int)(k0 / Ci), ci = (int)(k0 - (int64_t)tap * Ci);
+#pragma unroll
+      for (int i = 0; i < BK; ++i) {
+        float val = 0.0f;
+        if (k0 + i < k_end) {
+          const int kh = tap / kW, kw = tap - kh * kW;
+          const int hi = c.hi0 + kh, wi = c.wi0 + kw;
+          if ((unsigned)hi < (unsigned)H && (unsigned)wi < (unsigned)W)
+            val = __ldg(c.img + ((int64_t)hi * W + wi) * Ci + ci);
+        }
+        v[i] = val;
+        if (++ci == Ci) {
+          ci = 0;
+          ++tap;
+        }
+      }
+    }
+  }
+};
+
+// A of the input-gradient conv: row m = input pixel (n, hi, wi);
+// k = (kh, kw, co); value dy[n, ho, wo, co] when hi + pH - kh = ho*sH and
+// wi + pW - kw = wo*sW land inside the output (conv2d_kernels.cl:97-117).
+struct ConvDgradA {
+  const float* dy;
+  int64_t M;
+  int H, W, Co, kW, sH, sW, pH, pW, Ho, Wo;
+  bool vec;  // Co % 4 == 0 and dy 16-byte aligned
+  struct Ctx {
+    const float* img;
+    int hn0, wn0;
+    bool valid;
+  };
+  __device__ Ctx row(int64_t m) const {
+    Ctx c;
+    c.valid = m < M;
+    if (!c.valid) m = 0;
+    const int wi = (int)(m % W);
+    const int64_t t = m / W;
+    const int hi = (int)(t % H);
+    const int64_t n = t / H;
+    c.img = dy + n * Ho * Wo * Co;
+    c.hn0 = hi + pH;
+    c.wn0 = wi + pW;
+    return c;
+  }
+  __device__ __forceinline__ bool tap_src(const Ctx& c, int tap, int64_t* off) const {
+    const int kh = tap / kW, kw = tap - kh * kW;
+    const int hn = c.hn0 - kh, wn = c.wn0 - kw;
+    if (hn < 0 || wn < 0) return false;
+    const int ho = hn / sH, wo = wn / sW;
+    if (ho * sH != hn || wo * sW != wn || ho >= Ho || wo >= Wo) return false;
+    *off = ((int64_t)ho * Wo + wo) * Co;
+    return true;
+  }
+  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+    if (!c.valid) {
+      zero_row(v);
+      return;
+    }
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < BK / 4; ++q) {
+        const int64_t k = k0 + 4 * q;
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        int64_t off;
+        if (k < k_end) {
+          const int tap = (int)(k / Co), co = (int)(k - (int64_t)tap * Co);
+          if (tap_src(c, tap, &off)) t = __ldg(reinterpret_cast<const float4*>(c.img + off + co));
+        }
+        v[4 * q] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+      }
+    } else {
+      int tap = (int)(k0 / Co), co = (int)(k0 - (int64_t)tap * Co);
+      int64_t off = 0;
+      bool ok = tap_src(c, tap, &off);
+#pragma unroll
+      for (int i = 0; i < BK; ++i) {
+        v[i] = (k0 + i < k_end && ok) ? __ldg(c.img + off + co) : 0.0f;
+        if (++co == Co) {
+          co = 0;
+          ++tap;
+          ok = tap_src(c, tap, &off);
+        }
+      }
+    }
+  }
+};
+
+// B of the input-gradient conv: row n = ci; k = (tap, co); value
+// W[tap, ci, co] (HWIO).
+struct ConvDgradB {
+  const float* w;
+  int Ci, Co;
+  bool vec;  // Co % 4 == 0 and w 16-byte aligned
+  struct Ctx {
+    int ci;
+    bool valid;
+  };
+  __device__ Ctx row(int64_t n) const { return Ctx{(int)(n < Ci ? n : 0), n < Ci}; }
+  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+    if (!c.valid) {
+      zero_row(v);
+      return;
+    }
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < BK / 4; ++q) {
+        const int64_t k = k0 + 4 * q;
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < k_end) {
+          const int64_t tap = k / Co, co = k - tap * Co;
+          t = __ldg(reinterpret_cast<const float4*>(w + (tap * Ci + c.ci) * Co + co));
+        }
+        v[4 * q] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < BK; ++i) {
+        const int64_t k = k0 + i;
+        float val = 0.0f;
+        if (k < k_end) {
+          const int64_t tap = k / Co, co = k - tap * Co;
+          val = __ldg(w + (tap * Ci + c.ci) * Co + co);
+        }
+        v[i] = val;
+      }
+    }
+  }
+};
+
+// A of the filter-gradient conv: row m = (kh, kw, ci); k = output pixel p;
+// value x[n, ho*sH - pH + kh, wo*sW - pW + kw, ci] (conv2d_kernels.cl:143-156).
+struct ConvWgradA {
+  const float* x;
+  int64_t M;
+  int H, W, Ci, kW, sH, sW, pH, pW, Ho, Wo;
+  struct Ctx {
+    int kh, kw, ci;
+    bool valid;
+  };
+  __device__ Ctx row(int64_t m) const {
+    Ctx c;
+    c.valid = m < M;
+    if (!c.valid) m = 0;
+    const int tap = (int)(m / Ci);
+    c.ci = (int)(m - (int64_t)tap * Ci);
+    c.kh = tap / kW;
+    c.kw = tap - c.kh * kW;
+    return c;
+  }
+  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+    if (!c.valid) {
+      zero_row(v);
+      return;
+    }
+    int wo = (int)(k0 % Wo);
+    const int64_t t = k0 / Wo;
+    int ho = (int)(t % Ho);
+    int64_t n = t / Ho;
+#pragma unroll
+    for (int i = 0; i < BK; ++i) {
+      float val = 0.0f;
+      if (k0 + i < k_end) {
+        const int hi = ho * sH - pH + c.kh, wi = wo * sW - pW + c.kw;
+        if ((unsigned)hi < (unsigned)H && (unsigned)wi < (unsigned)W)
+          val = __ldg(x + ((n * H + hi) * W + wi) * Ci + c.ci);
+      }
+      v[i] = val;
+      if (++wo == Wo) {
+        wo = 0;
+        if (++ho == Ho) {
+          ho = 0;
+          ++n;
+        }
+      }
+    }
+  }
+};
+
+template <class AV, class BV>
+int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* out, const float* bias,
+             cudaStream_t s, const char* name, int min_kb_per_split = 4) {
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  if (M == 0 || N == 0) return B2_OK;
+  const int bn = choose_bn(N);
+  const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
+  int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);
+  int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
+  if (kps < BK) kps = BK;
+  splits = (int)(K > 0 ? ceil_div(K, kps) : 1);
+  B2_REQUIRE(tiles <= 65535LL * 2147483647LL && ceil_div(M, BM) <= 65535, "%s: problem too large", name);
+  GemmProblem<AV, BV> prob{a, b, M, N, K, kps, Epilogue{out, N, bias, false}};
+  if (splits == 1) return launch_gemm(prob, bn, 1, s, name);
+  Scratch part;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)splits * M * N, s));
+  prob.ep = Epilogue{part.as<float>(), N, nullptr, true};
+  B2_RETURN_IF_ERROR(launch_gemm(prob, bn, splits, s, name));
+  splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  return check_launch(s, "splitk_reduce");
+}
+
+// dense_kernels.cl:88-102: db[o] = sum_n dy[n, o], one thread per column in
+// the reference's order (bit-identical result).
+__global__ void dense_bias_grad_kernel(const float* __restrict__ dy, int64_t batch, int64_t out_f,
+                                       float* __restrict__ db) {
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= out_f) return;
+  float acc = 0.0f;
+  for (int64_t n = 0; n < batch; ++n) acc = __fadd_rn(acc, __ldg(dy + n * out_f + o));
+  db[o] = acc;
+}
+
+int conv_geom_fwd(const int64_t* input_shape, const int64_t* filter_shape, const int32_t* strides,
+                  int num_strides, const char* padding, bool forward, ConvGeom* g) {
+  B2_RETURN_IF_ERROR(check_dims_nonneg(input_shape, 4, "input"));
+  B2_RETURN_IF_ERROR(check_dims_nonneg(filter_shape, 4, "filter"));
+  B2_RETURN_IF_ERROR(parse_conv_attrs(strides, num_strides, padding, forward, g));
+  g->N = input_shape[0]; g->H = input_shape[1]; g->W = input_shape[2]; g->Ci = input_shape[3];
+  g->kH = filter_shape[0]; g->kW = filter_shape[1]; g->Co = filter_shape[3];
+  finish_geom(g);
+  return B2_OK;
+}
+
+bool is_pointwise(const ConvGeom& g) {
+  return g.kH == 1 && g.kW == 1 && g.sH == 1 && g.sW == 1 && g.pH == 0 && g.pW == 0;
+}
+
+}  // namespace tc
+}  // namespace b2
+
+using namespace b2;
+using namespace b2::tc;
+
+extern "C" {
+
+int b2_conv2d_output_shape(const int64_t input_shape[4], const int64_t filter_shape[4], const int32_t* strides,
+                           int num_strides, const char* padding, int64_t out_shape[4]) {
+  clear_error();
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(conv_geom_fwd(input_shape, filter_shape, strides, num_strides, padding, true, &g));
+  B2_REQUIRE(filter_shape[2] == input_shape[3], "filter[2] must equal input channels");
+  out_shape[0] = g.N; out_shape[1] = g.Ho; out_shape[2] = g.Wo; out_shape[3] = g.Co;
+  return B2_OK;
+}
+
+// src/ops/conv2d_ops.cc:107-190
+int b2_conv2d(b2_stream_t stream, const float* input, const int64_t input_shape[4], const float* filter,
+              const int64_t filter_shape[4], const int32_t* strides, int num_strides, const char* padding,
+              float* output, const int64_t output_shape[4]) {
+  clear_error();
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(conv_geom_fwd(input_shape, filter_shape, strides, num_strides, padding, true, &g));
+  B2_REQUIRE(filter_shape[2] == g.Ci, "filter[2] must equal input channels");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(output_shape, 4, "output"));
+  B2_REQUIRE(output_shape[0] == g.N && output_shape[1] == g.Ho && output_shape[2] == g.Wo && output_shape[3] == g.Co,
+             "output shape must be [%lld, %lld, %lld, %lld]", (long long)g.N, (long long)g.Ho, (long long)g.Wo,
+             (long long)g.Co);
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t M = g.N * g.Ho * g.Wo, K = g.kH * g.kW * g.Ci;
+  if (M == 0 || g.Co == 0) return B2_OK;
+  const MNMajor bv{filter, g.Co, g.Co};
+  if (is_pointwise(g)) {
+    const KContig av{input, M, g.Ci, aligned16(input) && g.Ci % 4 == 0};
+    return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_forward");
+  }
+  const ConvFpropA av{input, M, (int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW,
+                      (int)g.pH, (int)g.pW, (int)g.Ho, (int)g.Wo, aligned16(input) && g.Ci % 4 == 0};
+  return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_forward");
+}
+
+// src/ops/conv2d_ops.cc:225-314
+int b2_conv2d_backprop_input(b2_stream_t stream, const int32_t input_sizes[4], const float* filter,
+                             const int64_t filter_shape[4], const float* out_backprop,
+                             const int64_t out_backprop_shape[4], const int32_t* strides, int num_strides,
+                             const char* padding, float* output) {
+  clear_error();
+  B2_REQUIRE(input_sizes != nullptr, "input_sizes must have 4 elements");
+  const int64_t in_shape[4] = {input_sizes[0], input_sizes[1], input_sizes[2], input_sizes[3]};
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(conv_geom_fwd(in_shape, filter_shape, strides, num_strides, padding, false, &g));
+  B2_REQUIRE(filter_shape[2] == g.Ci, "filter[2] != Cin");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(out_backprop_shape, 4, "out_backprop"));
+  B2_REQUIRE(out_backprop_shape[0] == g.N && out_backprop_shape[1] == g.Ho && out_backprop_shape[2] == g.Wo &&
+                 out_backprop_shape[3] == g.Co,
+             "out_backprop shape mismatch");
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t M = g.N * g.H * g.W, K = g.kH * g.kW * g.Co;
+  if (M == 0 || g.Ci == 0) return B2_OK;
+  if (is_pointwise(g)) {
+    const KContig av{out_backprop, M, g.Co, aligned16(out_backprop) && g.Co % 4 == 0};
+    const KContig bv{filter, g.Ci, g.Co, aligned16(filter) && g.Co % 4 == 0};
+    return run_gemm(av, bv, M, g.Ci, K, output, nullptr, s, "conv2d_backprop_input");
+  }
+  const ConvDgradA av{out_backprop, M, (int)g.H, (int)g.W, (int)g.Co, (int)g.kW, (int)g.sH, (int)g.sW,
+                      (int)g.pH, (int)g.pW, (int)g.Ho, (int)g.Wo, aligned16(out_backprop) && g.Co % 4 == 0};
+  const ConvDgradB bv{filter, (int)g.Ci, (int)g.Co, aligned16(filter) && g.Co % 4 == 0};
+  return run_gemm(av, bv, M, g.Ci, K, output, nullptr, s, "conv2d_backprop_input");
+}
+
+// src/ops/conv2d_ops.cc:350-440
+int b2_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int64_t input_shape[4],
+                              const int32_t filter_sizes[4], const float* out_backprop,
+                              const int64_t out_backprop_shape[4], const int32_t* strides, int num_strides,
+                              const char* padding, float* output) {
+  clear_error();
+  B2_REQUIRE(filter_sizes != nullptr, "filter_sizes must have 4 elements");
+  const int64_t f_shape[4] = {filter_sizes[0], filter_sizes[1], filter_sizes[2], filter_sizes[3]};
+  ConvGeom g;
+  B2_RETURN_IF_ERROR(conv_geom_fwd(input_shape, f_shape, strides, num_strides, padding, false, &g));
+  B2_REQUIRE(input_shape[3] == f_shape[2], "input channels != filter_sizes[2]");
+  B2_RETURN_IF_ERROR(check_dims_nonneg(out_backprop_shape, 4, "out_backprop"));
+  B2_REQUIRE(out_backprop_shape[0] == g.N && out_backprop_shape[1] == g.Ho && out_backprop_shape[2] == g.Wo &&
+                 out_backprop_shape[3] == g.Co,
+             "out_backprop shape mismatch");
+  B2_RETURN_IF_ERROR(check_int32_sizes(g));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t M = g.kH * g.kW * g.Ci, K = g.N * g.Ho * g.Wo;
+  if (M == 0 || g.Co == 0) return B2_OK;
+  const MNMajor bv{out_backprop, g.Co, g.Co};
+  if (is_pointwise(g)) {
+    const MNMajor av{input, g.Ci, g.Ci};
+    return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_backprop_filter");
+  }
+  const ConvWgradA av{input, M, (int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW,
+                      (int)g.pH, (int)g.pW, (int)g.Ho, (int)g.Wo};
+  return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_backprop_filter");
+}
+
+// src/ops/dense_ops.cc:77-143
+int b2_dense(b2_stream_t stream, const float* x, const int64_t x_shape[2], const float* w, const int64_t w_shape[2],
+             const float* b, int64_t b_len, float* y) {
+  clear_error();
+  B2_REQUIRE(x_shape && w_shape, "x must be rank 2");
+  const int64_t batch = x_shape[0], in_f = x_shape[1], out_f = w_shape[1];
+  B2_REQUIRE(batch >= 0 && in_f >= 0 && out_f >= 0 && w_shape[0] >= 0, "dimensions must be non-negative");
+  B2_REQUIRE(w_shape[0] == in_f, "W[0] must equal x[1] (in_features)");
+  B2_REQUIRE(b_len == out_f, "b[0] must equal W[1] (out_features)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const KContig av{x, batch, in_f, aligned16(x) && in_f % 4 == 0};
+  const MNMajor bv{w, out_f, out_f};
+  return run_gemm(av, bv, batch, out_f, in_f, y, b, s, "dense_forward");
+}
+
+// src/ops/dense_ops.cc:170-227
+int b2_dense_backprop_input(b2_stream_t stream, const float* grad_y, const int64_t grad_y_shape[2], const float* w,
+                            const int64_t w_shape[2], float* grad_x) {
+  clear_error();
+  B2_REQUIRE(grad_y_shape && w_shape, "grad_y must be rank 2");
+  const int64_t batch = grad_y_shape[0], out_f = grad_y_shape[1], in_f = w_shape[0];
+  B2_REQUIRE(batch >= 0 && out_f >= 0 && in_f >= 0, "dimensions must be non-negative");
+  B2_REQUIRE(w_shape[1] == out_f, "W[1] must equal grad_y[1]");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const KContig av{grad_y, batch, out_f, aligned16(grad_y) && out_f % 4 == 0};
+  const KContig bv{w, in_f, out_f, aligned16(w) && out_f % 4 == 0};
+  return run_gemm(av, bv, batch, in_f, out_f, grad_x, nullptr, s, "dense_backprop_input");
+}
+
+// src/ops/dense_ops.cc:254-311
+int b2_dense_backprop_weight(b2_stream_t stream, const float* x, const int64_t x_shape[2], const float* grad_y,
+                             const int64_t grad_y_shape[2], float* grad_w) {
+  clear_error();
+  B2_REQUIRE(x_shape && grad_y_shape, "x must be rank 2");
+  const int64_t batch = x_shape[0], in_f = x_shape[1], out_f = grad_y_shape[1];
+  B2_REQUIRE(batch >= 0 && in_f >= 0 && out_f >= 0, "dimensions must be non-negative");
+  B2_REQUIRE(grad_y_shape[0] == batch, "x and grad_y must have the same batch size");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const MNMajor av{x, in_f, in_f};
+  const MNMajor bv{grad_y, out_f, out_f};
+  return run_gemm(av, bv, in_f, out_f, batch, grad_w, nullptr, s, "dense_backprop_weight");
+}
+
+// src/ops/dense_ops.cc:334-379
+int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_t grad_y_shape[2], float* grad_b) {
+  clear_error();
+  B2_REQUIRE(grad_y_shape, "grad_y must be rank 2");
+  const int64_t batch = grad_y_shape[0], out_f = grad_y_shape[1];
+  B2_REQUIRE(batch >= 0 && out_f >= 0, "dimensions must be non-negative");
+  if (out_f == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dense_bias_grad_kernel<<<(unsigned)ceil_div(out_f, 128), 128, 0, s>>>(grad_y, batch, out_f, grad_b);
+  return check_launch(s, "dense_backprop_bias");
+}
+
+// Number of bounded device-side waits that expired since load (tensor-core
+// kernels); the caller synchronises first.  Nonzero means a kernel gave up.
+int b2_device_timeouts(unsigned int* count) {
+  clear_error();
+  B2_CUDA_OR_RETURN(cudaMemcpyFromSymbol(count, g_tc_timeouts, sizeof(unsigned int)));
+  return B2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,170 @@
+"""Per-op timing and roofline accounting for a training step.
+
+``record_step(fn)`` runs ``fn()`` once (eagerly) while logging every op this
+library executes -- its name, the tensors and attrs it received -- and
+``time_ops(log)`` re-runs each logged call on its own: L2 is flushed (a
+256 MiB write) before every repetition and CUDA events on the current stream
+bracket the op only.  ``roofline(entry)`` gives each op's algorithmic work:
+
+* FLOPs = 2*M*N*K for the contractions (conv: 2*N*Ho*Wo*Co*kH*kW*Ci; dense
+  2*B*in*out), 2*taps per output for depthwise, 0 for the rest;
+* bytes = every input tensor read once + every output written once (fp32);
+
+and the binding ceiling: tensor cores when FLOPs/bytes exceeds the ridge
+(3xTF32 peak / HBM bandwidth), HBM otherwise.
+"""
+from __future__ import annotations
+
+import json
+import os
+from collections import defaultdict
+from pathlib import Path
+
+import torch
+
+from . import _library as L
+
+_KERNELS = ["_k_conv2d", "_k_conv2d_backprop_input", "_k_conv2d_backprop_filter", "_k_depthwise_conv2d",
+            "_k_depthwise_conv2d_backprop_input", "_k_depthwise_conv2d_backprop_filter", "_k_relu", "_k_relu_grad",
+            "_k_sigmoid", "_k_sigmoid_grad", "_k_batch_norm_training", "_k_batch_norm_inference",
+            "_k_batch_norm_grad", "_k_dense", "_k_dense_backprop_input", "_k_dense_backprop_weight",
+            "_k_dense_backprop_bias", "_k_upsampling_bilinear2d", "_k_upsampling_bilinear2d_grad"]
+
+
+def peaks(path=None) -> dict:
+    """Roofline denominators: the measured copy bandwidth and bf16 GEMM rate of
+    this pool's B200s when MEASURED_PEAKS.json is present, else fallbacks."""
+    p = Path(path) if path else Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:  # noqa: BLE001
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def tf32x3_peak_tflops(pk: dict) -> float:
+    """Algorithmic FLOP/s ceiling of 3xTF32: TF32 runs at half the bf16 rate
+    and every product costs three MMAs."""
+    return pk["bf16_tflops"] / 2.0 / 3.0
+
+
+def record_step(fn):
+    """Run ``fn()`` with every library op logged; returns (result, log)."""
+    log = []
+    saved = {}
+    for name in _KERNELS:
+        orig = getattr(L, name)
+        saved[name] = orig
+
+        def wrap(*args, _orig=orig, _name=name, **kw):
+            out = _orig(*args, **kw)
+            log.append((_name[3:], _orig, args, kw, out))
+            return out
+
+        setattr(L, name, wrap)
+    try:
+        res = fn()
+    finally:
+        for name, orig in saved.items():
+            setattr(L, name, orig)
+    return res, log
+
+
+def _numel(t):
+    return t.numel() if isinstance(t, torch.Tensor) else 0
+
+
+def work(name, args, kw, out) -> tuple[float, float]:
+    """(algorithmic FLOPs, algorithmic bytes) of one logged op call."""
+    outs = out if isinstance(out, tuple) else (out,)
+    tin = [a for a in list(args) + list(kw.values()) if isinstance(a, torch.Tensor)]
+    byts = 4.0 * (sum(_numel(t) for t in tin) + sum(_numel(t) for t in outs))
+    flops = 0.0
+    if name in ("conv2d", "conv2d_backprop_input", "conv2d_backprop_filter"):
+        if name == "conv2d":
+            y, w = outs[0], args[1]
+            flops = 2.0 * y.numel() * w.shape[0] * w.shape[1] * w.shape[2]
+        elif name == "conv2d_backprop_input":
+            w, dy = args[1], args[2]
+            flops = 2.0 * dy.numel() * w.shape[0] * w.shape[1] * w.shape[2]
+        else:
+            dy, dw = args[2], outs[0]
+            flops = 2.0 * dy.numel() * dw.shape[0] * dw.shape[1] * dw.shape[2]
+    elif name.startswith("depthwise"):
+        w = args[1] if name != "depthwise_conv2d_backprop_filter" else outs[0]
+        taps = w.shape[0] * w.shape[1]
+        big = outs[0] if name == "depthwise_conv2d" else args[2]
+        flops = 2.0 * big.numel() * taps
+    elif name == "dense":
+        x, w = args[0], args[1]
+        flops = 2.0 * x.shape[0] * x.shape[1] * w.shape[1]
+    elif name == "dense_backprop_input":
+        dy, w = args[0], args[1]
+        flops = 2.0 * dy.shape[0] * dy.shape[1] * w.shape[0]
+    elif name == "dense_backprop_weight":
+        x, dy = args[0], args[1]
+        flops = 2.0 * x.shape[0] * x.shape[1] * dy.shape[1]
+    return flops, byts
+
+
+class _Flusher:
+    def __init__(self, device, mib=256):
+        self.buf = torch.empty(mib * (1 << 20) // 4, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_call(fn, reps=5, flush=None) -> float:
+    """Mean device milliseconds of ``fn()`` over ``reps`` runs (events on the
+    current stream around the call only; ``flush()`` runs between)."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    fn()  # warm
+    for i in range(reps):
+        if flush:
+            flush()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / reps
+
+
+def time_ops(log, reps=5, device=None) -> list[dict]:
+    """Times every logged op call; returns one dict per call."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    flush = _Flusher(dev)
+    pk = peaks()
+    tc_peak = tf32x3_peak_tflops(pk) * 1e12
+    ridge = tc_peak / (pk["hbm_gbs"] * 1e9)
+    rows = []
+    for name, orig, args, kw, out in log:
+        ms = time_call(lambda: orig(*args, **kw), reps=reps, flush=flush)
+        flops, byts = work(name, args, kw, out)
+        bound = "tensor" if byts > 0 and flops / byts > ridge else "hbm"
+        if bound == "tensor":
+            ach, peak, unit = flops / (ms * 1e-3) / 1e12, tc_peak / 1e12, "TFLOP/s"
+        else:
+            ach, peak, unit = byts / (ms * 1e-3) / 1e9, pk["hbm_gbs"], "GB/s"
+        rows.append({"op": name, "ms": ms, "flops": flops, "bytes": byts, "bound": bound, "achieved": ach,
+                     "peak": peak, "unit": unit, "frac": ach / peak if peak else 0.0})
+    return rows
+
+
+def summarize(rows) -> dict:
+    """Aggregate per op type: total ms, call count, time-weighted roofline fraction."""
+    agg = defaultdict(lambda: {"ms": 0.0, "calls": 0, "wfrac": 0.0})
+    for r in rows:
+        a = agg[r["op"]]
+        a["ms"] += r["ms"]
+        a["calls"] += 1
+        a["wfrac"] += r["frac"] * r["ms"]
+    out = {}
+    for k, a in sorted(agg.items(), key=lambda kv: -kv[1]["ms"]):
+        out[k] = {"ms": round(a["ms"], 4), "calls": a["calls"], "frac": round(a["wfrac"] / a["ms"], 3) if a["ms"] else 0}
+    return out
+
+

@@ -1,0 +1,103 @@
+"""BatchNorm parity on the GPU (reference tests: tests/test_batchnorm.py).
+The per-channel reductions run in a different order than the reference's
+serial loop, so statistics and reductions are within the fp32 tolerance;
+given identical statistics the elementwise passes are bit-exact."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_bitexact, assert_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def _inputs(seed, shape):
+    rng = np.random.default_rng(seed)
+    C = shape[-1]
+    x = rng.standard_normal(shape).astype(np.float32)
+    g = (rng.standard_normal(C) + 1.0).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    return x, g, b
+
+
+@pytest.mark.parametrize("shape", [(4, 7, 7, 8), (2, 5, 5, 6), (3, 5, 5, 4), (1, 1, 1, 3), (2, 3, 3, 1),
+                                   (8, 16, 16, 48), (4, 9, 7, 144), (2, 4, 4, 1100)])
+def test_bn_training_forward(otf, port, shape):
+    x, g, b = _inputs(0, shape)
+    y, m, v = (to_np(t) for t in otf.batch_norm_training(_cuda(x), _cuda(g), _cuda(b)))
+    ry, rm, rv = port.batch_norm_training(x, g, b)
+    assert_close(m, rm, what="mean")
+    assert_close(v, rv, what="var")
+    assert_close(y, ry, what="y")
+    # given the GPU's statistics the normalisation is the reference formula bit for bit
+    assert_bitexact(y, port.batch_norm_inference(x, g, b, m, v), "normalize")
+
+
+def test_bn_inference_forward_bitexact(otf, port):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((2, 5, 5, 6)).astype(np.float32)
+    g = (rng.standard_normal(6) + 1.0).astype(np.float32)
+    b = (rng.standard_normal(6) * 0.1).astype(np.float32)
+    m = (rng.standard_normal(6) * 0.5).astype(np.float32)
+    v = (np.abs(rng.standard_normal(6)) + 0.1).astype(np.float32)
+    got = to_np(otf.batch_norm_inference(_cuda(x), _cuda(g), _cuda(b), _cuda(m), _cuda(v)))
+    assert_bitexact(got, port.batch_norm_inference(x, g, b, m, v), "bn inference")
+
+
+@pytest.mark.parametrize("shape", [(3, 5, 5, 4), (4, 7, 7, 8), (8, 16, 16, 48), (2, 3, 3, 5)])
+def test_bn_grad(otf, port, shape):
+    x, g, _ = _inputs(2, shape)
+    dy = np.random.default_rng(5).standard_normal(shape).astype(np.float32)
+    _, m, v = port.batch_norm_training(x, g, np.zeros_like(g))
+    gx, gg, gb = (to_np(t) for t in otf.batch_norm_grad(_cuda(dy), _cuda(x), _cuda(g), _cuda(m), _cuda(v)))
+    rx, rg, rb = port.batch_norm_grad(dy, x, g, m, v)
+    assert_close(gb, rb, what="grad_beta")
+    assert_close(gg, rg, what="grad_gamma")
+    assert_close(gx, rx, what="grad_x")
+
+
+def test_bn_training_gradients_via_autograd(otf, port):
+    x, g, b = _inputs(2, (3, 5, 5, 4))
+    xt, gt, bt = (_cuda(a).requires_grad_(True) for a in (x, g, b))
+    y, _, _ = otf.batch_norm_training(xt, gt, bt)
+    (0.5 * (y * y).sum()).backward()
+    ry, rm, rv = port.batch_norm_training(x, g, b)
+    rx, rg, rb = port.batch_norm_grad(ry, x, g, rm, rv)
+    assert_close(to_np(xt.grad), rx, what="dx")
+    assert_close(to_np(gt.grad), rg, what="dgamma")
+    assert_close(to_np(bt.grad), rb, what="dbeta")
+
+
+def test_bn_inference_has_no_gradient(otf):
+    x = torch.randn(1, 2, 2, 3, device="cuda", requires_grad=True)
+    c = torch.ones(3, device="cuda")
+    y = otf.batch_norm_inference(x, c, c * 0, c * 0, c)
+    with pytest.raises(LookupError):
+        y.sum().backward()
+
+
+def test_bn_deterministic(otf):
+    x = torch.randn(64, 32, 16, 48, device="cuda")
+    g, b = torch.ones(48, device="cuda"), torch.zeros(48, device="cuda")
+    a = otf.batch_norm_training(x, g, b)
+    c = otf.batch_norm_training(x, g, b)
+    for u, w in zip(a, c):
+        assert torch.equal(u, w)
+
+
+def test_bn_bad_shapes(otf):
+    x = torch.zeros(1, 2, 2, 3, device="cuda")
+    with pytest.raises(otf.errors.InvalidArgumentError, match="gamma/beta size must equal channels"):
+        otf.batch_norm_training(x, torch.ones(4, device="cuda"), torch.zeros(3, device="cuda"))
+    with pytest.raises(otf.errors.InvalidArgumentError, match="NHWC"):
+        otf.batch_norm_training(torch.zeros(2, 3, device="cuda"), torch.ones(3, device="cuda"),
+                                torch.zeros(3, device="cuda"))
+    with pytest.raises(otf.errors.InvalidArgumentError, match="matching NHWC shapes"):
+        otf.batch_norm_grad(torch.zeros(1, 2, 2, 4, device="cuda"), x, torch.ones(3, device="cuda"),
+                            torch.zeros(3, device="cuda"), torch.ones(3, device="cuda"))

@@ -1,0 +1,131 @@
+"""End-to-end: the README build_model() network's training step on the GPU
+against the oracle-composed step (tests/netoracle.py) -- loss, output and
+every weight gradient -- plus the CUDA-graph step and convergence checks
+(the reference's "loss decreases" integration tests)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, rel_errs, to_np
+from oracle.netstep import params_of, train_grads
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(seed=0):
+    from opencl_tf.model import build_model
+    torch.manual_seed(seed)
+    return build_model(device="cuda")
+
+
+def _batch(n, seed=1):
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(0, 1, (n, 64, 64, 3)).astype(np.float32)
+    t = rng.uniform(0, 1, (n, 8, 8, 8)).astype(np.float32)
+    return x, t
+
+
+def test_build_model_step_matches_oracle(otf, port):
+    from opencl_tf.train import mse
+    m = _model()
+    x, t = _batch(4)
+    p = params_of(m)
+    out = m(torch.from_numpy(x).cuda(), training=True)
+    loss = mse(out, torch.from_numpy(t).cuda())
+    loss.backward()
+    r_loss, r_out, r_g = train_grads(port, p, x, t)
+    assert abs(float(loss) - r_loss) <= 1e-5 * abs(r_loss)
+    assert_close(to_np(out), r_out, what="output")
+    pairs = [("stem_w", m.stem_conv.kernel), ("stem_g", m.stem_bn.gamma), ("stem_b", m.stem_bn.beta),
+             ("dense_w", m.dense.kernel), ("dense_b", m.dense.bias)]
+    for i, (dw, bn1, _, pw, bn2, _) in enumerate(m.blocks):
+        gb = r_g["blocks"][i]
+        pairs += [(("blocks", i, "dw"), dw.kernel), (("blocks", i, "g1"), bn1.gamma), (("blocks", i, "b1"), bn1.beta),
+                  (("blocks", i, "pw"), pw.kernel), (("blocks", i, "g2"), bn2.gamma), (("blocks", i, "b2"), bn2.beta)]
+    worst = []
+    for key, param in pairs:
+        want = r_g[key] if isinstance(key, str) else r_g["blocks"][key[1]][key[2]]
+        mx, l2 = rel_errs(to_np(param.grad), want)
+        worst.append((mx, l2, key))
+        assert mx <= 1e-4 and l2 <= 1e-5, (key, mx, l2)
+
+
+def test_graphed_step_equals_eager_step(otf):
+    from opencl_tf.train import TrainStep
+    x, t = _batch(8, seed=2)
+    xd, td = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
+    m1, m2 = _model(3), _model(3)
+    eager = TrainStep(m1, graphed=False)
+    graphed = TrainStep(m2, graphed=True, warmup=3)
+    for _ in range(3):
+        eager(xd, td)
+    l_g = graphed(xd, td)  # 3 warm-up steps + the captured step
+    l_e = eager(xd, td)
+    torch.cuda.synchronize()
+    assert torch.equal(l_g, l_e)
+    for a, b in zip(m1.parameters(), m2.parameters()):
+        assert torch.equal(a, b)
+    for _ in range(3):
+        l_g, l_e = graphed(xd, td), eager(xd, td)
+    assert torch.equal(l_g, l_e)
+
+
+def test_loss_decreases(otf):
+    from opencl_tf.train import TrainStep
+    x, t = _batch(16, seed=4)
+    xd, td = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
+    step = TrainStep(_model(5), lr=1e-3, graphed=True)
+    first = float(step(xd, td))
+    for _ in range(20):
+        last = float(step(xd, td))
+    assert last < first, (first, last)
+
+
+def test_bn_moving_stats_update(otf):
+    bn = otf.layers.OpenCLBatchNormalization(momentum=0.5)
+    _ = bn(torch.zeros(1, 2, 2, 3, device="cuda"), training=False)
+    m0, v0 = bn.moving_mean.clone(), bn.moving_var.clone()
+    rng = np.random.default_rng(0)
+    for _ in range(4):
+        bn(torch.from_numpy(rng.standard_normal((4, 3, 3, 3)).astype(np.float32) * 3 + 1).cuda(), training=True)
+    assert not torch.allclose(bn.moving_mean, m0)
+    assert not torch.allclose(bn.moving_var, v0)
+
+
+@pytest.mark.parametrize("layer_fn", ["conv", "dw", "dense", "sigmoid", "bn"])
+def test_keras_like_layers_train(otf, layer_fn):
+    """Each layer inside an SGD step: loss decreases (reference
+    test_keras_layer_trains pattern)."""
+    L = otf.layers
+    torch.manual_seed(42)
+    if layer_fn == "conv":
+        layer, x, tgt = L.OpenCLConv2D(4, 3), torch.randn(2, 8, 8, 3), torch.randn(2, 8, 8, 4)
+    elif layer_fn == "dw":
+        layer, x, tgt = L.OpenCLDepthwiseConv2D(3), torch.randn(2, 8, 8, 3), torch.randn(2, 8, 8, 3)
+    elif layer_fn == "dense":
+        layer, x, tgt = L.OpenCLDense(8), torch.randn(8, 16), torch.randn(8, 8)
+    elif layer_fn == "sigmoid":
+        layer, x, tgt = L.OpenCLSigmoid(), torch.randn(2, 4, 4, 8), torch.rand(2, 4, 4, 8)
+        x.requires_grad_(True)
+    else:
+        layer, x, tgt = L.OpenCLBatchNormalization(), torch.randn(4, 5, 5, 3) * 2 + 1, torch.randn(4, 5, 5, 3)
+    x, tgt = x.cuda(), tgt.cuda()
+    if layer_fn == "sigmoid":
+        x = x.detach().requires_grad_(True)
+    _ = layer(x)
+    params = list(layer.parameters()) or [x]
+    opt = torch.optim.SGD(params, lr=1e-2 if layer_fn != "sigmoid" else 1.0)
+
+    def step():
+        opt.zero_grad()
+        loss = torch.mean((layer(x) - tgt) ** 2)
+        loss.backward()
+        opt.step()
+        return float(loss)
+
+    l0 = step()
+    for _ in range(5):
+        l1 = step()
+    assert l1 < l0
