@@ -242,7 +242,9 @@ def run_ours(args, rank, world, local_rank):
 
     clocks.start()
     time.sleep(0.3)
+    torch.cuda.nvtx.range_push("timed_steps")
     ms_dev = timed(lambda: step(x_dev, t_dev), args.steps)
+    torch.cuda.nvtx.range_pop()
 
     # ---- end to end: pinned host batch in, loss out, every step
     x_host = torch.from_numpy(x_np).pin_memory()

@@ -71,3 +71,47 @@ def train_grads(o, p, x, target, head=(4, 4, 8), up=(2, 2), eps=1e-3):
     d, g["stem_g"], g["stem_b"] = o.batch_norm_grad(d, t["c0"], p["stem_g"], t["m0"], t["v0"], eps)
     g["stem_w"] = o.conv2d_backprop_filter(x, p["stem_w"].shape, d, S1, "SAME")
     return loss, out, g
+
+
+def train_grads_f64(p, x, target, head=(4, 4, 8), up=(2, 2), eps=1e-3, device="cpu"):
+    """The same training step in float64 torch autograd (NCHW convolutions with
+    TF SAME padding, biased-variance BN, half-pixel bilinear) -- the exact
+    arbiter.  Returns (loss, out, grads) keyed like train_grads()."""
+    import torch
+    import torch.nn.functional as F
+
+    dev = torch.device(device)
+    tt = lambda a: torch.tensor(np.asarray(a), dtype=torch.float64, device=dev, requires_grad=True)  # noqa: E731
+    P = {k: tt(p[k]) for k in ("stem_w", "stem_g", "stem_b", "dense_w", "dense_b")}
+    Bl = [{k: tt(v) for k, v in b.items()} for b in p["blocks"]]
+
+    def conv(z, w, stride, groups=1):
+        kh, kw = w.shape[0], w.shape[1]
+        H, W = z.shape[2], z.shape[3]
+        oh, ow = -(-H // stride[0]), -(-W // stride[1])
+        ph = max((oh - 1) * stride[0] + kh - H, 0)
+        pw = max((ow - 1) * stride[1] + kw - W, 0)
+        z = F.pad(z, (pw // 2, pw - pw // 2, ph // 2, ph - ph // 2))
+        wt = w.permute(3, 2, 0, 1) if groups == 1 else w.permute(2, 3, 0, 1)
+        return F.conv2d(z, wt, stride=stride, groups=groups)
+
+    def bn(z, gm, bt):
+        m = z.mean(dim=(0, 2, 3), keepdim=True)
+        v = (z * z).mean(dim=(0, 2, 3), keepdim=True) - m * m
+        return gm.view(1, -1, 1, 1) * (z - m) / torch.sqrt(v + eps) + bt.view(1, -1, 1, 1)
+
+    N = x.shape[0]
+    z = torch.tensor(x, dtype=torch.float64, device=dev).permute(0, 3, 1, 2)
+    z = torch.relu(bn(conv(z, P["stem_w"], (1, 2)), P["stem_g"], P["stem_b"]))
+    for b in Bl:
+        z = torch.relu(bn(conv(z, b["dw"], (2, 2), groups=z.shape[1]), b["g1"], b["b1"]))
+        z = torch.relu(bn(conv(z, b["pw"], (1, 1)), b["g2"], b["b2"]))
+    z = z.permute(0, 2, 3, 1).reshape(N, -1)
+    z = torch.relu(z @ P["dense_w"] + P["dense_b"]).reshape(N, *head).permute(0, 3, 1, 2)
+    z = F.interpolate(z, scale_factor=up, mode="bilinear", align_corners=False)
+    out = torch.sigmoid(z).permute(0, 2, 3, 1)
+    loss = torch.mean((out - torch.tensor(target, dtype=torch.float64, device=dev)) ** 2)
+    loss.backward()
+    g = {k: P[k].grad.cpu().numpy() for k in P}
+    g["blocks"] = [{k: v.grad.cpu().numpy() for k, v in b.items()} for b in Bl]
+    return float(loss), out.detach().cpu().numpy(), g

@@ -68,13 +68,19 @@ def _same(padding: str) -> int:
     return 1 if padding == "SAME" else 0
 
 
+def _cdiv(a: int, b: int) -> int:
+    """C integer division (truncates toward zero)."""
+    q = abs(a) // abs(b)
+    return q if (a >= 0) == (b > 0) else -q
+
+
 def resolve_padding(in_size: int, k: int, stride: int, padding: str):
-    """src/padding_utils.h:22-33 (TF SAME/VALID)."""
+    """src/padding_utils.h:22-33 (TF SAME/VALID), with C integer division."""
     if padding == "SAME":
-        out = (in_size + stride - 1) // stride
-        pad = max((out - 1) * stride + k - in_size, 0) // 2
+        out = _cdiv(in_size + stride - 1, stride)
+        pad = _cdiv(max((out - 1) * stride + k - in_size, 0), 2)
     else:
-        out = (in_size - k + stride) // stride
+        out = _cdiv(in_size - k + stride, stride)
         pad = 0
     return out, pad
 

@@ -63,13 +63,17 @@ def test_bn_grad(otf, port, shape):
 
 
 def test_bn_training_gradients_via_autograd(otf, port):
+    """loss = 0.5*sum(y^2) as in the reference test (tests/test_batchnorm.py:71-101).
+    Its true input gradient is ~0 (|y| is invariant to x), so dx is rounding
+    noise on both sides; like the reference test, dx is compared with an
+    absolute tolerance.  gamma / beta gradients are well conditioned."""
     x, g, b = _inputs(2, (3, 5, 5, 4))
     xt, gt, bt = (_cuda(a).requires_grad_(True) for a in (x, g, b))
     y, _, _ = otf.batch_norm_training(xt, gt, bt)
     (0.5 * (y * y).sum()).backward()
     ry, rm, rv = port.batch_norm_training(x, g, b)
     rx, rg, rb = port.batch_norm_grad(ry, x, g, rm, rv)
-    assert_close(to_np(xt.grad), rx, what="dx")
+    np.testing.assert_allclose(to_np(xt.grad), rx, atol=1e-4, rtol=1e-4)
     assert_close(to_np(gt.grad), rg, what="dgamma")
     assert_close(to_np(bt.grad), rb, what="dbeta")
 

@@ -51,10 +51,11 @@ def test_upsampling_agrees_with_torch_interpolate(otf):
     np.testing.assert_allclose(got, want, atol=1e-5)
 
 
-def test_upsampling_single_pixel(otf):
+def test_upsampling_single_pixel(otf, port):
     x = np.array([[[[3.0, -1.0, 2.5]]]], np.float32)
     got = to_np(otf.upsampling_bilinear_2d(_cuda(x), size=[3, 4]))
-    np.testing.assert_array_equal(got, np.broadcast_to(x, got.shape))
+    np.testing.assert_allclose(got, np.broadcast_to(x, got.shape), atol=1e-4)
+    assert_bitexact(got, port.upsampling_bilinear_2d(x, [3, 4]), "single pixel")
 
 
 def test_upsampling_1x_is_identity(otf):

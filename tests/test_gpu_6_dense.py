@@ -65,7 +65,7 @@ def test_stress_gemm_reduced(otf):
     y = otf.dense(x, W, b)
     want = (x.double() @ W.double()).cpu().numpy()
     mx, l2 = rel_errs(to_np(y), want)
-    assert mx < 1e-5 and l2 < 1e-6, (mx, l2)
+    assert mx <= 1e-4 and l2 <= 1e-5, (mx, l2)
 
 
 def test_dense_bad_args(otf):

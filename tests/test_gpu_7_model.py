@@ -27,29 +27,49 @@ def _batch(n, seed=1):
     return x, t
 
 
-def test_build_model_step_matches_oracle(otf, port):
+def _grad_pairs(m, g):
+    out = [("stem_w", m.stem_conv.kernel, g["stem_w"]), ("stem_g", m.stem_bn.gamma, g["stem_g"]),
+           ("stem_b", m.stem_bn.beta, g["stem_b"]), ("dense_w", m.dense.kernel, g["dense_w"]),
+           ("dense_b", m.dense.bias, g["dense_b"])]
+    for i, (dw, bn1, _, pw, bn2, _) in enumerate(m.blocks):
+        gb = g["blocks"][i]
+        out += [(f"b{i}.dw", dw.kernel, gb["dw"]), (f"b{i}.g1", bn1.gamma, gb["g1"]), (f"b{i}.b1", bn1.beta, gb["b1"]),
+                (f"b{i}.pw", pw.kernel, gb["pw"]), (f"b{i}.g2", bn2.gamma, gb["g2"]), (f"b{i}.b2", bn2.beta, gb["b2"])]
+    return out
+
+
+@pytest.mark.parametrize("batch", [2, 4, 8])
+def test_build_model_step_matches_oracle(otf, port, batch):
+    """Loss, output and all 17 weight gradients.  Each gradient must be within
+    the contract tolerance of the oracle (the reference's arithmetic); where
+    the oracle itself is farther than that from the float64 answer (the
+    stem and first depthwise filter gradients: BN backward amplifies the
+    rounding of the reference's long serial sums), the GPU must instead be
+    within the tolerance of float64 and no farther from it than the oracle."""
     from opencl_tf.train import mse
+    from oracle.netstep import train_grads_f64
     m = _model()
-    x, t = _batch(4)
+    x, t = _batch(batch)
     p = params_of(m)
     out = m(torch.from_numpy(x).cuda(), training=True)
     loss = mse(out, torch.from_numpy(t).cuda())
     loss.backward()
     r_loss, r_out, r_g = train_grads(port, p, x, t)
-    assert abs(float(loss) - r_loss) <= 1e-5 * abs(r_loss)
+    e_loss, e_out, e_g = train_grads_f64(p, x, t, device="cuda")
+    assert abs(float(loss.detach()) - r_loss) <= 1e-5 * abs(r_loss)
     assert_close(to_np(out), r_out, what="output")
-    pairs = [("stem_w", m.stem_conv.kernel), ("stem_g", m.stem_bn.gamma), ("stem_b", m.stem_bn.beta),
-             ("dense_w", m.dense.kernel), ("dense_b", m.dense.bias)]
-    for i, (dw, bn1, _, pw, bn2, _) in enumerate(m.blocks):
-        gb = r_g["blocks"][i]
-        pairs += [(("blocks", i, "dw"), dw.kernel), (("blocks", i, "g1"), bn1.gamma), (("blocks", i, "b1"), bn1.beta),
-                  (("blocks", i, "pw"), pw.kernel), (("blocks", i, "g2"), bn2.gamma), (("blocks", i, "b2"), bn2.beta)]
-    worst = []
-    for key, param in pairs:
-        want = r_g[key] if isinstance(key, str) else r_g["blocks"][key[1]][key[2]]
-        mx, l2 = rel_errs(to_np(param.grad), want)
-        worst.append((mx, l2, key))
-        assert mx <= 1e-4 and l2 <= 1e-5, (key, mx, l2)
+    report = []
+    for (name, param, want), (_, _, exact) in zip(_grad_pairs(m, r_g), _grad_pairs(m, e_g)):
+        got = to_np(param.grad)
+        vs_ref, ref_vs_exact, vs_exact = rel_errs(got, want), rel_errs(want, exact), rel_errs(got, exact)
+        report.append((name, vs_ref, ref_vs_exact, vs_exact))
+        if vs_ref[0] <= 1e-4 and vs_ref[1] <= 1e-5:
+            continue
+        assert ref_vs_exact[0] > 1e-4 or ref_vs_exact[1] > 1e-5, (name, vs_ref, ref_vs_exact)
+        assert vs_exact[0] <= 1e-4 and vs_exact[1] <= 1e-5, (name, vs_exact, ref_vs_exact)
+        assert vs_exact[1] <= ref_vs_exact[1], (name, vs_exact, ref_vs_exact)
+    print("\n".join(f"{n:8s} gpu-vs-oracle {a[0]:.1e}/{a[1]:.1e}  oracle-vs-f64 {b[0]:.1e}/{b[1]:.1e}  "
+                    f"gpu-vs-f64 {c[0]:.1e}/{c[1]:.1e}" for n, a, b, c in report))
 
 
 def test_graphed_step_equals_eager_step(otf):
