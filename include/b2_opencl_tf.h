@@ -192,6 +192,25 @@ int b2_batch_norm_training(b2_stream_t stream, const float* x,
                            int64_t beta_len, float epsilon, float* y,
                            float* saved_mean, float* saved_var);
 
+/* Same computation and outputs as b2_batch_norm_training, for callers that
+ * must not have device memory allocated during a call -- a runtime whose
+ * memory manager owns all of HBM, or a warm serving loop that cannot accept
+ * an allocation's synchronisation and latency.  It has no counterpart in the
+ * reference.  Its reduction scratch is a fixed 256 KiB array in the library's
+ * device image (held on every GPU that loads the library until exit), so it
+ * accepts at most 16384 channels and returns B2_ERR_INVALID_ARGUMENT beyond
+ * that.  The first call on each device looks up that array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the array: calls whose work overlaps on the GPU
+ * (different streams, no ordering between them) race and corrupt each
+ * other's statistics, so order them (e.g. issue them on one stream). */
+int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* x,
+                                    const int64_t x_shape[4],
+                                    const float* gamma, int64_t gamma_len,
+                                    const float* beta, int64_t beta_len,
+                                    float epsilon, float* y, float* saved_mean,
+                                    float* saved_var);
+
 /* OpenclBatchNormInference(x, gamma, beta, mean, var; epsilon) -> y
  * src/ops/batchnorm_ops.cc:192-282 */
 int b2_batch_norm_inference(b2_stream_t stream, const float* x,

@@ -18,6 +18,8 @@
 // reference formulas with round-to-nearest intrinsics (no contraction) and
 // inv_std = 1/sqrt(var+eps) in IEEE fp32, so, given the same statistics,
 // y and grad_x are bit-identical to the reference's formula.
+#include <mutex>
+
 #include "b2_internal.cuh"
 
 namespace b2 {
@@ -427,3 +429,90 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t gr
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// BatchNorm training forward that allocates nothing.
+//
+// Some callers cannot let a library allocate device memory during a call:
+// runtimes whose memory manager owns all of HBM (a framework that reserves
+// its arena at start-up and accounts for every byte), or latency-critical
+// serving loops where an allocation's possible device-wide synchronisation
+// and unbounded cost are not acceptable once the process is warm.  For them
+// this variant keeps its reduction partials in a fixed array that is part of
+// the library's device image instead of taking them from the pool.
+//
+// Limit: 256 KiB of scratch per GPU (kNoAllocScratch float2 entries), held by
+// every device that loads the library until the process exits.  Inputs need
+// at most kNoAllocMaxChannels channels; the row blocks of the reduction are
+// capped so that blocks * C partials plus C per-channel constants fit.
+// ===========================================================================
+
+namespace {
+constexpr int kNoAllocScratch = 32768;        // float2 entries = 256 KiB
+constexpr int kNoAllocMaxChannels = 16384;
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+
+// Device scratch of the allocation-free entry point.  In host code this name
+// is only a handle for cudaGetSymbolAddress, never a device address.
+static __device__ __align__(256) float2 g_bn_no_alloc_scratch[kNoAllocScratch];
+
+namespace {
+std::once_flag g_no_alloc_once[kNoAllocMaxDevices];
+void* g_no_alloc_addr[kNoAllocMaxDevices];
+cudaError_t g_no_alloc_status[kNoAllocMaxDevices];
+
+// Runs once per device, with that device current.
+void resolve_no_alloc_scratch(int dev) {
+  g_no_alloc_status[dev] = cudaGetSymbolAddress(&g_no_alloc_addr[dev], g_bn_no_alloc_scratch);
+}
+}  // namespace
+
+extern "C" int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* x, const int64_t x_shape[4],
+                                               const float* gamma, int64_t gamma_len, const float* beta,
+                                               int64_t beta_len, float epsilon, float* y, float* saved_mean,
+                                               float* saved_var) {
+  using namespace b2;
+  clear_error();
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  const int64_t C = x_shape[3];
+  B2_REQUIRE(gamma_len == C && beta_len == C, "gamma/beta size must equal channels");
+  B2_REQUIRE(C <= kNoAllocMaxChannels,
+             "b2_batch_norm_training_no_alloc supports at most %d channels (got %lld); "
+             "use b2_batch_norm_training", kNoAllocMaxChannels, (long long)C);
+  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
+  const int64_t total = rows * C;
+  if (C == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  const int dev = d->device;
+  B2_REQUIRE(dev < kNoAllocMaxDevices, "device ordinal %d out of range", dev);
+  std::call_once(g_no_alloc_once[dev], resolve_no_alloc_scratch, dev);
+  if (g_no_alloc_status[dev] != cudaSuccess)
+    return set_error(B2_ERR_INTERNAL, "cudaGetSymbolAddress of the static scratch failed (cuda_err=%d: %s)",
+                     (int)g_no_alloc_status[dev], cudaGetErrorString(g_no_alloc_status[dev]));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  // Partials take blocks * C entries, the per-channel inv_std ceil(C/2) more.
+  const int64_t fit = (kNoAllocScratch - ceil_div(C, 2)) / C;
+  int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  if (blocks > fit) blocks = (int)fit;
+  float2* partial = static_cast<float2*>(g_no_alloc_addr[dev]);
+  float* inv = reinterpret_cast<float*>(partial + (int64_t)blocks * C);
+  // Every scratch entry read below is written earlier in this call, so no
+  // clearing is needed; the previous call's contents are simply overwritten.
+  dim3 grid(blocks, geo.chunks);
+  if (geo.vec == 4)
+    bn_partial_kernel<4, 0><<<grid, kThreads, 0, s>>>(x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, geo,
+                                                        partial);
+  else
+    bn_partial_kernel<1, 0><<<grid, kThreads, 0, s>>>(x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, geo,
+                                                        partial);
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_reduce_stats (no alloc)"));
+  bn_stats_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(partial, blocks, (int)C, rows, epsilon,
+                                                                       saved_mean, saved_var, inv);
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize (no alloc)"));
+  if (total == 0) return B2_OK;
+  return launch_normalize(s, x, saved_mean, inv, gamma, beta, y, total, (int)C, vec_ok);
+}
