@@ -37,9 +37,12 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
   }
 }
 
+// N tile: the whole N when it fits in kMaxBN columns, else balanced tiles of
+// at most 128 (multiples of 16, the UMMA N granularity at M = 128).
 int choose_bn(int64_t N) {
-  if (N <= 256) return (int)(ceil_div(N < 16 ? 16 : N, 16) * 16);
-  return N >= 2048 ? 256 : 128;
+  if (N <= kMaxBN) return (int)(ceil_div(N < 16 ? 16 : N, 16) * 16);
+  const int64_t tiles = ceil_div(N, 128);
+  return (int)(ceil_div(ceil_div(N, tiles), 16) * 16);
 }
 
 int choose_stages(int bn, int max_smem) {
@@ -74,24 +77,24 @@ struct ConvFpropA {
   __device__ Ctx row(int64_t m) const {
     Ctx c;
     c.valid = m < M;
-    if (!c.valid) m = 0;
-    const int wo = (int)(m % Wo);
-    const int64_t t = m / Wo;
-    const int ho = (int)(t % Ho);
-    const int64_t n = t / Ho;
-    c.img = x + n * H * W * Ci;
+    const uint32_t mm = c.valid ? (uint32_t)m : 0u;  // M < 2^31 (checked on the host)
+    const uint32_t t = mm / (uint32_t)Wo;
+    const int wo = (int)(mm - t * (uint32_t)Wo);
+    const uint32_t n = t / (uint32_t)Ho;
+    const int ho = (int)(t - n * (uint32_t)Ho);
+    c.img = x + (int64_t)n * H * W * Ci;
     c.hi0 = ho * sH - pH;
     c.wi0 = wo * sW - pW;
     return c;
   }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
     if (vec) {
 #pragma unroll
-      for (int q = 0; q < BK / 4; ++q) {
+      for (int q = 0; q < kUnit / 4; ++q) {
         const int64_t k = k0 + 4 * q;
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         if (k < k_end) {
@@ -107,20 +110,25 @@ struct ConvFpropA {
         v[4 * q + 3] = t.w;
       }
     } else {
-      int tap = (int)(k0 / Ci), ci = (int)(k0 - (int64_t)tap * Ci);
+      // walk (kh, kw, ci) from k0 without dividing per element
+      const uint32_t tap0 = (uint32_t)k0 / (uint32_t)Ci;
+      int ci = (int)((uint32_t)k0 - tap0 * (uint32_t)Ci);
+      int kh = (int)(tap0 / (uint32_t)kW), kw = (int)(tap0 - (uint32_t)kh * (uint32_t)kW);
 #pragma unroll
-      for (int i = 0; i < BK; ++i) {
+      for (int i = 0; i < kUnit; ++i) {
         float val = 0.0f;
         if (k0 + i < k_end) {
-          const int kh = tap / kW, kw = tap - kh * kW;
           const int hi = c.hi0 + kh, wi = c.wi0 + kw;
           if ((unsigned)hi < (unsigned)H && (unsigned)wi < (unsigned)W)
-            val = __ldg(c.img + ((int64_t)hi * W + wi) * Ci + ci);
+            val = __ldg(c.img + (hi * W + wi) * Ci + ci);
         }
         v[i] = val;
         if (++ci == Ci) {
           ci = 0;
-          ++tap;
+          if (++kw == kW) {
+            kw = 0;
+            ++kh;
+          }
         }
       }
     }
@@ -162,14 +170,14 @@ struct ConvDgradA {
     *off = ((int64_t)ho * Wo + wo) * Co;
     return true;
   }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
     if (vec) {
 #pragma unroll
-      for (int q = 0; q < BK / 4; ++q) {
+      for (int q = 0; q < kUnit / 4; ++q) {
         const int64_t k = k0 + 4 * q;
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         int64_t off;
@@ -187,7 +195,7 @@ struct ConvDgradA {
       int64_t off = 0;
       bool ok = tap_src(c, tap, &off);
 #pragma unroll
-      for (int i = 0; i < BK; ++i) {
+      for (int i = 0; i < kUnit; ++i) {
         v[i] = (k0 + i < k_end && ok) ? __ldg(c.img + off + co) : 0.0f;
         if (++co == Co) {
           co = 0;
@@ -210,14 +218,14 @@ struct ConvDgradB {
     bool valid;
   };
   __device__ Ctx row(int64_t n) const { return Ctx{(int)(n < Ci ? n : 0), n < Ci}; }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
     if (vec) {
 #pragma unroll
-      for (int q = 0; q < BK / 4; ++q) {
+      for (int q = 0; q < kUnit / 4; ++q) {
         const int64_t k = k0 + 4 * q;
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         if (k < k_end) {
@@ -231,7 +239,7 @@ struct ConvDgradB {
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < BK; ++i) {
+      for (int i = 0; i < kUnit; ++i) {
         const int64_t k = k0 + i;
         float val = 0.0f;
         if (k < k_end) {
@@ -264,22 +272,22 @@ struct ConvWgradA {
     c.kw = tap - c.kh * kW;
     return c;
   }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
-    int wo = (int)(k0 % Wo);
-    const int64_t t = k0 / Wo;
-    int ho = (int)(t % Ho);
-    int64_t n = t / Ho;
+    const uint32_t t = (uint32_t)k0 / (uint32_t)Wo;  // pixel count < 2^31 (checked on the host)
+    int wo = (int)((uint32_t)k0 - t * (uint32_t)Wo);
+    uint32_t n = t / (uint32_t)Ho;
+    int ho = (int)(t - n * (uint32_t)Ho);
 #pragma unroll
-    for (int i = 0; i < BK; ++i) {
+    for (int i = 0; i < kUnit; ++i) {
       float val = 0.0f;
       if (k0 + i < k_end) {
         const int hi = ho * sH - pH + c.kh, wi = wo * sW - pW + c.kw;
         if ((unsigned)hi < (unsigned)H && (unsigned)wi < (unsigned)W)
-          val = __ldg(x + ((n * H + hi) * W + wi) * Ci + c.ci);
+          val = __ldg(x + (((int64_t)n * H + hi) * W + wi) * Ci + c.ci);
       }
       v[i] = val;
       if (++wo == Wo) {
@@ -305,13 +313,12 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
   int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
   if (kps < BK) kps = BK;
   splits = (int)(K > 0 ? ceil_div(K, kps) : 1);
-  B2_REQUIRE(tiles <= 65535LL * 2147483647LL && ceil_div(M, BM) <= 65535, "%s: problem too large", name);
-  GemmProblem<AV, BV> prob{a, b, M, N, K, kps, Epilogue{out, N, bias, false}};
-  if (splits == 1) return launch_gemm(prob, bn, 1, s, name);
+  GemmProblem<AV, BV> prob{a, b, M, N, K, kps, splits, Epilogue{out, N, bias, false}};
+  if (splits == 1) return launch_gemm(prob, bn, s, name);
   Scratch part;
   B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)splits * M * N, s));
   prob.ep = Epilogue{part.as<float>(), N, nullptr, true};
-  B2_RETURN_IF_ERROR(launch_gemm(prob, bn, splits, s, name));
+  B2_RETURN_IF_ERROR(launch_gemm(prob, bn, s, name));
   splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
   return check_launch(s, "splitk_reduce");
 }

@@ -1,34 +1,48 @@
-// tc_gemm.cuh -- 3xTF32 GEMM engine on the sm_100a tensor cores (tcgen05).
+// tc_gemm.cuh -- persistent 3xTF32 GEMM engine on the sm_100a tensor cores.
 //
-// Computes D[M,N] = sum_k A[m,k] * B[k,n] in fp32-class accuracy for every
+// Computes D[M,N] = sum_k A[m,k] * B[k,n] with fp32-class accuracy for every
 // contraction on the hot path (Dense forward / backward, implicit-GEMM Conv2D
-// forward / input grad / filter grad).  A "problem" object describes how to
-// gather one tile row of A or B from global memory, so the same engine runs
-// plain row-major matrices, transposed operands and im2col views.
+// forward / input grad / filter grad).  An operand "view" says how to gather
+// a piece of one tile row of A or B from global memory, so the same engine
+// runs row-major matrices, transposed operands and im2col views without
+// materialising them.
 //
-// Per CTA: one 128 x BN output tile (BN a multiple of 16, <= 256), K walked in
-// 32-element blocks through a ring of shared-memory stages.
+// Output tiles are 128 x BN (BN a multiple of 16, <= 256); K is walked in
+// 32-element blocks through a ring of shared-memory stages; split-K slices
+// are extra tiles.  One CTA per SM loops over tiles (static round robin),
+// with three warp roles:
 //
-//   warps 0-3  producers: each thread owns one tile row of A (and one or two
-//              of B), loads its 32 fp32 values, splits each into
-//              hi = tf32(x), lo = tf32(x - hi) (round to nearest) and stores
-//              both into K-major, no-swizzle UMMA layouts; then
-//              fence.proxy.async + mbarrier arrive on the stage's FULL barrier.
-//   warp 4     allocates the TMEM accumulator; lane 0 waits FULL, issues
-//              per 8-wide k step  D += Ahi*Bhi + Ahi*Blo + Alo*Bhi
-//              (tcgen05.mma.cta_group::1.kind::tf32, M=128, N=BN) and
-//              tcgen05.commit's the stage's EMPTY barrier; a final commit
-//              arms the ACCUM barrier.
-//   epilogue   warps 0-3 read their 32 TMEM lanes (tcgen05.ld 32x32b) and
-//              write rows of D (optionally + bias), or fp32 partials for a
-//              split-K reduction.
+//   warps 0-7   producers.  A stage holds (128 + BN) rows x 32 k of fp32;
+//               each thread owns fixed 8-element pieces of 2 A rows and up to
+//               4 B rows, loads them, splits x = hi + lo (hi = tf32(x),
+//               lo = tf32(x - hi), round to nearest) and stores both into
+//               K-major no-swizzle UMMA layouts (conflict-free: the 8 lanes
+//               of a quarter warp write one 128-byte core matrix), then
+//               fence.proxy.async and arrive on the stage's FULL barrier.
+//   warp 8      allocates TMEM: two chunk accumulators P0, P1 and a running
+//               sum S, BN fp32 columns each.  Lane 0 waits FULL and issues, per
+//               8-wide k step, P += Alo*Bhi + Ahi*Blo + Ahi*Bhi
+//               (tcgen05.mma.cta_group::1.kind::tf32, M=128, N=BN), commits
+//               each stage's EMPTY barrier, and after at most kChunkKB
+//               k-blocks commits the chunk (CHUNK_FULL) and switches to the
+//               other P.
+//   warps 9-12  epilogue.  Per chunk: wait CHUNK_FULL, read their 32 TMEM
+//               lanes of P (tcgen05.ld 32x32b), add the running sum S in fp32
+//               with round-to-nearest, and either write S back (tcgen05.st) or,
+//               after the tile's last chunk, store rows of D (+ bias) or fp32
+//               split-K partials; then release P (CHUNK_EMPTY) while the MMA
+//               warp fills the other one.
 //
-// Error-compensated 3xTF32 (the dropped lo*lo term is ~2^-22 relative) keeps
-// fp32 accuracy; accumulation is fp32 in TMEM.
+// Why chunks: the tensor core's fp32 accumulation rounds on every update, so
+// the error of one accumulator grows with the number of k steps it absorbs
+// (measured ~7e-9 relative per k).  Folding every 256 k into S with
+// round-to-nearest adds keeps long reductions (filter gradients over
+// 500k pixels, K = 4096 GEMMs) at fp32-class accuracy; tiles whose K fits in
+// one chunk go straight from P to global memory.
 //
 // Every mbarrier wait is bounded by a wall-clock limit; on expiry the thread
-// records the failure in g_tc_timeouts and leaves its loop, the CTA still
-// frees its TMEM, and the host reports B2_ERR_TIMEOUT when it checks.
+// counts the event in g_tc_timeouts (read by b2_device_timeouts()) and the
+// CTA stops issuing work, still frees its TMEM and exits.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -40,11 +54,16 @@
 namespace b2 {
 namespace tc {
 
-constexpr int BM = 128;             // UMMA M (cta_group::1)
-constexpr int BK = 32;              // fp32 elements of K per stage (128 B rows)
-constexpr int kProducerWarps = 4;
-constexpr int kThreads = 32 * (kProducerWarps + 1);
+constexpr int BM = 128;  // UMMA M (cta_group::1)
+constexpr int BK = 32;   // fp32 elements of K per stage
+constexpr int kProducerWarps = 8;
+constexpr int kMmaWarp = kProducerWarps;
+constexpr int kEpiWarp0 = kProducerWarps + 1;
+constexpr int kThreads = 32 * (kProducerWarps + 1 + 4);
 constexpr int kMaxStages = 6;
+constexpr int kUnit = 8;  // k elements per producer unit
+constexpr int kChunkKB = 8;  // k-blocks accumulated in one TMEM chunk (256 k)
+constexpr int kMaxBN = 160;  // three BN-column regions must fit in 512 TMEM columns
 constexpr uint64_t kWaitLimitNs = 10ull * 1000 * 1000 * 1000;  // 10 s
 
 // Count of bounded waits that expired, read by the host through
@@ -84,16 +103,20 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Bounded wait for `parity` on `bar`; false (and a recorded timeout) if the
-// phase did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase of parity `parity` on `bar`.  On expiry: count
+// the timeout, raise the CTA's abort flag and return false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
-      atomicAdd(&g_tc_timeouts, 1u);
-      return false;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        atomicAdd(&g_tc_timeouts, 1u);
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
@@ -104,10 +127,9 @@ __device__ __forceinline__ uint32_t tf32_rna(float x) {
   return r;
 }
 
-// K-major, no-swizzle canonical layout ((8,n),2):((16B,SBO),LBO):
-// core matrices of 8 rows x 16 B; LBO = 128 B between the core matrices that
-// are adjacent along K, SBO = 1024 B between 8-row groups (8 core matrices
-// cover one 32-element K block).  Element (r, k) of a tile lives at
+// K-major, no-swizzle canonical layout ((8,n),2):((16B,SBO),LBO): core
+// matrices of 8 rows x 16 B; LBO = 128 B between core matrices adjacent along
+// K, SBO = 1024 B between 8-row groups.  Element (r, k) of a tile lives at
 //   (r/8)*1024 + (k/4)*128 + (r%8)*16 + (k%4)*4   bytes.
 constexpr uint32_t kLBO = 128;
 constexpr uint32_t kSBO = 1024;
@@ -135,6 +157,17 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
@@ -148,11 +181,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Split 32 values of tile row `r` into hi/lo tf32 and store them.
-__device__ __forceinline__ void store_row_split(uint8_t* hi_tile, uint8_t* lo_tile, int r, const float (&v)[BK]) {
-  const uint32_t row_off = (uint32_t)(r >> 3) * kSBO + (uint32_t)(r & 7) * 16u;
+// Split 8 values (k offsets 8q..8q+7) of tile row r into hi/lo tf32 and store.
+__device__ __forceinline__ void store_unit_split(uint8_t* hi_tile, uint8_t* lo_tile, int r, int q,
+                                                 const float (&v)[kUnit]) {
+  const uint32_t off = (uint32_t)(r >> 3) * kSBO + (uint32_t)(2 * q) * kLBO + (uint32_t)(r & 7) * 16u;
 #pragma unroll
-  for (int c = 0; c < BK / 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -160,23 +194,23 @@ __device__ __forceinline__ void store_row_split(uint8_t* hi_tile, uint8_t* lo_ti
       h[j] = tf32_rna(x);
       l[j] = tf32_rna(x - __uint_as_float(h[j]));
     }
-    *reinterpret_cast<uint4*>(hi_tile + row_off + c * kLBO) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(lo_tile + row_off + c * kLBO) = make_uint4(l[0], l[1], l[2], l[3]);
+    *reinterpret_cast<uint4*>(hi_tile + off + c * kLBO) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_tile + off + c * kLBO) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
-__device__ __forceinline__ void zero_row(float (&v)[BK]) {
+__device__ __forceinline__ void zero_unit(float (&v)[kUnit]) {
 #pragma unroll
-  for (int i = 0; i < BK; ++i) v[i] = 0.0f;
+  for (int i = 0; i < kUnit; ++i) v[i] = 0.0f;
 }
 
 // --------------------------------------------------------- operand views
 //
 // A view exposes, for tile row r (an M index for A, an N index for B):
-//   Ctx row(int r) const;                      per-row state, computed once
-//   void load(const Ctx&, int k0, int k_end, float (&v)[32]) const;
-// filling v[i] = op(r, k0 + i) for k0 + i < k_end, 0 otherwise (and 0 for
-// rows outside the matrix).
+//   Ctx row(int64_t r) const;                          per-row state
+//   void load8(const Ctx&, int64_t k, int64_t k_end, float (&v)[8]) const;
+// filling v[i] = op(r, k + i) for k + i < k_end, 0 otherwise, and 0 for
+// rows outside the matrix.  k is a multiple of 8.
 
 // op(r, k) = p[r * ld + k]   (K contiguous)
 struct KContig {
@@ -188,23 +222,19 @@ struct KContig {
     bool valid;
   };
   __device__ Ctx row(int64_t r) const { return Ctx{p + r * ld, r < rows}; }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
-    if (vec && k0 + BK <= k_end) {
-#pragma unroll
-      for (int q = 0; q < BK / 4; ++q) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(c.base + k0) + q);
-        v[4 * q] = t.x;
-        v[4 * q + 1] = t.y;
-        v[4 * q + 2] = t.z;
-        v[4 * q + 3] = t.w;
-      }
+    if (vec && k + kUnit <= k_end) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(c.base + k));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(c.base + k) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < BK; ++i) v[i] = (k0 + i < k_end) ? __ldg(c.base + k0 + i) : 0.0f;
+      for (int i = 0; i < kUnit; ++i) v[i] = (k + i < k_end) ? __ldg(c.base + k + i) : 0.0f;
     }
   }
 };
@@ -218,13 +248,13 @@ struct MNMajor {
     bool valid;
   };
   __device__ Ctx row(int64_t r) const { return Ctx{p + r, r < rows}; }
-  __device__ void load(const Ctx& c, int64_t k0, int64_t k_end, float (&v)[BK]) const {
+  __device__ void load8(const Ctx& c, int64_t k, int64_t k_end, float (&v)[kUnit]) const {
     if (!c.valid) {
-      zero_row(v);
+      zero_unit(v);
       return;
     }
 #pragma unroll
-    for (int i = 0; i < BK; ++i) v[i] = (k0 + i < k_end) ? __ldg(c.base + (k0 + i) * ld) : 0.0f;
+    for (int i = 0; i < kUnit; ++i) v[i] = (k + i < k_end) ? __ldg(c.base + (k + i) * ld) : 0.0f;
   }
 };
 
@@ -232,10 +262,10 @@ struct MNMajor {
 
 // How results leave the accumulator.
 struct Epilogue {
-  float* out;          // D, row-major, leading dimension ldo (or partials)
+  float* out;         // D, row-major, leading dimension ldo (or partials)
   int64_t ldo;
-  const float* bias;   // optional per-column bias (direct mode only)
-  bool partial;        // write split z to out + z * M * N (ld = N), no bias
+  const float* bias;  // optional per-column bias (direct mode only)
+  bool partial;       // write split z to out + z * M * N (ld = N), no bias
 };
 
 template <class AV, class BV>
@@ -244,6 +274,7 @@ struct GemmProblem {
   BV b;
   int64_t M, N, K;
   int64_t k_per_split;  // multiple of BK
+  int splits;
   Epilogue ep;
 };
 
@@ -261,8 +292,29 @@ inline KernelSmem smem_plan(int bn, int stages) {
   s.b_bytes = (size_t)bn * BK * 4;
   s.stage_bytes = 2 * s.a_bytes + 2 * s.b_bytes;
   s.bar_offset = s.stage_bytes * stages;
-  s.total = s.bar_offset + 8 * (2 * kMaxStages + 1) + 16 + 1024;  // + alignment slack
+  s.total = s.bar_offset + 8 * (2 * kMaxStages + 4) + 16 + 1024;  // + alignment slack
   return s;
+}
+
+struct TileCoord {
+  int64_t m0, n0, k_begin, k_end;
+  int z, nkb;
+};
+
+template <class P>
+__device__ __forceinline__ TileCoord tile_coord(const P& p, int bn, int64_t t) {
+  const int64_t nt = (p.N + bn - 1) / bn, mt = (p.M + BM - 1) / BM;
+  TileCoord c;
+  const int64_t n_idx = t % nt;
+  const int64_t rest = t / nt;
+  c.m0 = (rest % mt) * BM;
+  c.z = (int)(rest / mt);
+  c.n0 = n_idx * bn;
+  c.k_begin = (int64_t)c.z * p.k_per_split;
+  c.k_end = c.k_begin + p.k_per_split;
+  if (c.k_end > p.K) c.k_end = p.K;
+  c.nkb = c.k_end > c.k_begin ? (int)((c.k_end - c.k_begin + BK - 1) / BK) : 0;
+  return c;
 }
 
 template <class P>
@@ -274,19 +326,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
   const size_t stage_bytes = 2 * a_bytes + 2 * b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stage_bytes * stages);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* accum = empty + kMaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* chunk_full = empty + kMaxStages;  // [2]
+  uint64_t* chunk_empty = chunk_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
   __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * bn;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
-  const int64_t k_begin = (int64_t)blockIdx.z * p.k_per_split;
-  int64_t k_end = k_begin + p.k_per_split;
-  if (k_end > p.K) k_end = p.K;
-  const int nkb = k_end > k_begin ? (int)((k_end - k_begin + BK - 1) / BK) : 0;
-  const uint32_t tmem_cols = bn <= 32 ? 32u : bn <= 64 ? 64u : bn <= 128 ? 128u : 256u;
+  const int64_t nt = (p.N + bn - 1) / bn, mt = (p.M + BM - 1) / BM;
+  const int64_t tiles = nt * mt * p.splits;
+  const uint32_t acc_cols = (uint32_t)bn;
+  const int need_cols = 3 * bn;  // P0, P1, S
+  const uint32_t tmem_cols = need_cols <= 32 ? 32u : need_cols <= 64 ? 64u : need_cols <= 128 ? 128u
+                             : need_cols <= 256 ? 256u : 512u;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -294,10 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
       mbar_init(&full[s], kProducerWarps * 32);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&chunk_full[a], 1);
+      mbar_init(&chunk_empty[a], 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kProducerWarps) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(tmem_cols)
                  : "memory");
@@ -310,98 +366,167 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
 
   if (warp < kProducerWarps) {
     // ---------------------------------------------------------- producers
-    const int t = threadIdx.x;
-    const auto ca = p.a.row(m0 + t);
-    const auto cb0 = p.b.row(n0 + t);
-    const auto cb1 = p.b.row(n0 + t + 128);
-    float v[BK];
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % stages;
-      const uint32_t ph = (uint32_t)(kb / stages) & 1u;
-      if (kb >= stages && !mbar_wait(&empty[s], ph ^ 1u)) {
-        s_abort = 1;
-        break;
+    // Thread (warp w, lane l): rows 8w + (l & 7) (+64 per unit), k piece q = l >> 3.
+    const int rsub = 8 * warp + (lane & 7);
+    const int q = lane >> 3;
+    uint32_t stage_cnt = 0;
+    for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, bn, t);
+      const auto ca0 = p.a.row(tc.m0 + rsub);
+      const auto ca1 = p.a.row(tc.m0 + rsub + 64);
+      typename decltype(p.b)::Ctx cb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cb[j] = p.b.row(tc.n0 + rsub + 64 * j);
+      for (int kb = 0; kb < tc.nkb; ++kb, ++stage_cnt) {
+        const int s = (int)(stage_cnt % (uint32_t)stages);
+        const uint32_t round = stage_cnt / (uint32_t)stages;
+        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) break;
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        const int64_t k = tc.k_begin + (int64_t)kb * BK + q * kUnit;
+        float v0[kUnit], v1[kUnit];
+        p.a.load8(ca0, k, tc.k_end, v0);
+        p.a.load8(ca1, k, tc.k_end, v1);
+        store_unit_split(st, st + a_bytes, rsub, q, v0);
+        store_unit_split(st, st + a_bytes, rsub + 64, q, v1);
+        uint8_t* bhi = st + 2 * a_bytes;
+        uint8_t* blo = bhi + b_bytes;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          const int r0 = rsub + 64 * j, r1 = r0 + 64;
+          if (r0 < bn) {
+            if (tc.n0 + r0 < p.N) p.b.load8(cb[j], k, tc.k_end, v0); else zero_unit(v0);
+          }
+          if (r1 < bn) {
+            if (tc.n0 + r1 < p.N) p.b.load8(cb[j + 1], k, tc.k_end, v1); else zero_unit(v1);
+          }
+          if (r0 < bn) store_unit_split(bhi, blo, r0, q, v0);
+          if (r1 < bn) store_unit_split(bhi, blo, r1, q, v1);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&full[s]);
       }
-      if (s_abort) break;
-      uint8_t* st = smem + (size_t)s * stage_bytes;
-      const int64_t k0 = k_begin + (int64_t)kb * BK;
-      p.a.load(ca, k0, k_end, v);
-      store_row_split(st, st + a_bytes, t, v);
-      if (t < bn) {
-        if (n0 + t < p.N) p.b.load(cb0, k0, k_end, v); else zero_row(v);
-        store_row_split(st + 2 * a_bytes, st + 2 * a_bytes + b_bytes, t, v);
-      }
-      if (t + 128 < bn) {
-        if (n0 + t + 128 < p.N) p.b.load(cb1, k0, k_end, v); else zero_row(v);
-        store_row_split(st + 2 * a_bytes, st + 2 * a_bytes + b_bytes, t + 128, v);
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&full[s]);
     }
-  } else if (lane == 0) {
+  } else if (warp == kMmaWarp) {
     // -------------------------------------------------------- MMA issuer
-    const uint32_t idesc = idesc_tf32(bn);
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(bn);
+      uint32_t stage_cnt = 0, g = 0;  // g counts chunks
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = tile_coord(p, bn, t);
+        for (int kb0 = 0; kb0 < tc.nkb && ok; kb0 += kChunkKB, ++g) {
+          const int a = (int)(g & 1u);
+          const uint32_t use = g >> 1;
+          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
+          const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
+          for (int kb = kb0; kb < kb1; ++kb, ++stage_cnt) {
+            const int s = (int)(stage_cnt % (uint32_t)stages);
+            if (!mbar_wait(&full[s], (stage_cnt / (uint32_t)stages) & 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+            const uint32_t a_hi = st, a_lo = st + (uint32_t)a_bytes;
+            const uint32_t b_hi = st + 2u * (uint32_t)a_bytes, b_lo = b_hi + (uint32_t)b_bytes;
+#pragma unroll
+            for (int j = 0; j < BK / 8; ++j) {
+              const uint32_t off = (uint32_t)j * 2u * kLBO;  // 8 tf32 = two core matrices along K
+              mma_tf32(d, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+              mma_tf32(d, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
+              mma_tf32(d, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
+            }
+            mma_commit(&empty[s]);
+          }
+          mma_commit(&chunk_full[a]);
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_off + 2u * acc_cols;
+    uint32_t g = 0;
     bool ok = true;
-    for (int kb = 0; kb < nkb && ok; ++kb) {
-      const int s = kb % stages;
-      const uint32_t ph = (uint32_t)(kb / stages) & 1u;
-      if (!mbar_wait(&full[s], ph)) {
-        s_abort = 1;
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
-      const uint32_t a_hi = st, a_lo = st + (uint32_t)a_bytes;
-      const uint32_t b_hi = st + 2u * (uint32_t)a_bytes, b_lo = b_hi + (uint32_t)b_bytes;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, bn, t);
+      const int64_t m = tc.m0 + quarter * 32 + lane;
+      const int64_t n_lim = p.N - tc.n0 < bn ? p.N - tc.n0 : bn;
+      const int nch = (tc.nkb + kChunkKB - 1) / kChunkKB;
+      for (int ch = 0; ch < (nch > 0 ? nch : 1); ++ch) {
+        const bool first = ch == 0, last = ch + 1 >= nch;
+        const int a = (int)(g & 1u);
+        if (nch > 0) {
+          if (!mbar_wait(&chunk_full[a], (g >> 1) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        const uint32_t p_addr = tmem_base + lane_off + (uint32_t)a * acc_cols;
+        for (int c = 0; c < bn; c += 16) {
+          float v[16];
+          if (nch > 0) {
+            tmem_ld16(p_addr + (uint32_t)c, v);
+            if (!first) {
+              float sv[16];
+              tmem_ld16(s_addr + (uint32_t)c, sv);
 #pragma unroll
-      for (int j = 0; j < BK / 8; ++j) {
-        const uint32_t off = (uint32_t)j * 2u * kLBO;  // 8 tf32 = two core matrices along K
-        mma_tf32(tmem_base, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, (kb > 0 || j > 0) ? 1u : 0u);
-        mma_tf32(tmem_base, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
-        mma_tf32(tmem_base, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
-      }
-      mma_commit(&empty[s]);
-    }
-    mma_commit(accum);
-  }
-
-  // ------------------------------------------------------------- epilogue
-  if (warp < kProducerWarps) {
-    const int64_t m = m0 + warp * 32 + lane;
-    bool have_acc = nkb > 0;
-    if (have_acc && !mbar_wait(accum, 0)) {
-      s_abort = 1;
-      have_acc = false;
-    }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int64_t n_lim = p.N - n0 < bn ? p.N - n0 : bn;
-    for (int c = 0; c < bn; c += 16) {
-      float v[16];
-      if (have_acc) {
-        tmem_ld16(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-      } else {
+              for (int e = 0; e < 16; ++e) v[e] = __fadd_rn(sv[e], v[e]);
+            }
+          } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-      }
-      if (m >= p.M || c >= n_lim) continue;
-      if (p.ep.partial) {
-        float* dst = p.ep.out + (int64_t)blockIdx.z * p.M * p.N + m * p.N + n0 + c;
+            for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+          }
+          if (!last) {
+            tmem_st16(s_addr + (uint32_t)c, v);
+            continue;
+          }
+          if (m >= p.M || c >= n_lim) continue;
+          float* dst;
+          const float* bias = nullptr;
+          int64_t ld;
+          if (p.ep.partial) {
+            dst = p.ep.out + (int64_t)tc.z * p.M * p.N + m * p.N + tc.n0 + c;
+            ld = p.N;
+          } else {
+            dst = p.ep.out + m * p.ep.ldo + tc.n0 + c;
+            ld = p.ep.ldo;
+            if (p.ep.bias) bias = p.ep.bias + tc.n0 + c;
+          }
+          if (bias) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (c + i < n_lim) dst[i] = v[i];
-      } else {
-        float* dst = p.ep.out + m * p.ep.ldo + n0 + c;
-        const float* bias = p.ep.bias ? p.ep.bias + n0 + c : nullptr;
+            for (int e = 0; e < 16; ++e)
+              if (c + e < n_lim) v[e] += __ldg(bias + e);
+          }
+          if (c + 16 <= n_lim && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) && (ld % 4 == 0)) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (c + i < n_lim) dst[i] = bias ? v[i] + __ldg(bias + i) : v[i];
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < n_lim) dst[e] = v[e];
+          }
+        }
+        if (nch > 0) {
+          if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          mbar_arrive(&chunk_empty[a]);  // P may be refilled
+          ++g;
+        }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == kProducerWarps) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
@@ -413,13 +538,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N,
                                      const float* __restrict__ bias, float* __restrict__ out, int64_t ldo);
 
-// Launch helpers (tc_gemm.cu).
+// Launch helpers (gemm_ops.cu).
 int choose_bn(int64_t N);
 int choose_stages(int bn, int max_smem);
 int splits_for(int64_t tiles, int64_t K, int sm_count, int min_kb_per_split);
 
 template <class P>
-int launch_gemm(P prob, int bn, int splits, cudaStream_t s, const char* name) {
+int launch_gemm(P prob, int bn, cudaStream_t s, const char* name) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   const int stages = choose_stages(bn, d->max_smem_optin);
@@ -430,7 +555,8 @@ int launch_gemm(P prob, int bn, int splits, cudaStream_t s, const char* name) {
         cudaFuncSetAttribute(tc_gemm_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.total));
     configured_bytes = (int)plan.total;
   }
-  dim3 grid((unsigned)ceil_div(prob.N, bn), (unsigned)ceil_div(prob.M, BM), (unsigned)splits);
+  const int64_t tiles = ceil_div(prob.N, bn) * ceil_div(prob.M, BM) * prob.splits;
+  const int grid = (int)(tiles < d->sm_count ? tiles : d->sm_count);
   tc_gemm_kernel<P><<<grid, kThreads, plan.total, s>>>(prob, bn, stages);
   return check_launch(s, name);
 }
