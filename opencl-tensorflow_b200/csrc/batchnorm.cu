@@ -61,6 +61,7 @@ template <>
 struct VecT<1> {
   using T = float;
   __device__ static void to(const T& v, float* o) { o[0] = v; }
+  __device__ static void from(const float* o, T* p) { *p = o[0]; }
 };
 template <>
 struct VecT<4> {
@@ -71,6 +72,7 @@ struct VecT<4> {
     o[2] = v.z;
     o[3] = v.w;
   }
+  __device__ static void from(const float* o, T* p) { *p = make_float4(o[0], o[1], o[2], o[3]); }
 };
 
 // Stage 1.  MODE 0: (sum x, sum x^2).  MODE 1: (sum dy, sum dy * x_hat) with
@@ -116,7 +118,38 @@ __global__ void __launch_bounds__(kThreads)
 
   if (active) {
     const int loc = cg_local * VEC;
-    for (int64_t r = r_begin + r_off; r < r_end; r += geo.rpi) {
+    float m[VEC], inv[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      m[j] = MODE == 1 ? s_mean[loc + j] : 0.0f;
+      inv[j] = MODE == 1 ? s_inv[loc + j] : 0.0f;
+    }
+    constexpr int U = 4;  // rows per thread per iteration: U (or 2U) independent loads in flight
+    const int64_t step = (int64_t)geo.rpi;
+    int64_t r = r_begin + r_off;
+    for (; r + (U - 1) * step < r_end; r += U * step) {
+      float v[U][VEC], g[U][VEC];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        VecT<VEC>::to(*reinterpret_cast<const V*>(x + (r + u * step) * C + c0), v[u]);
+        if (MODE == 1) VecT<VEC>::to(*reinterpret_cast<const V*>(dy + (r + u * step) * C + c0), g[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          if (MODE == 0) {
+            acc_a[j] += v[u][j];
+            acc_b[j] = fmaf(v[u][j], v[u][j], acc_b[j]);
+          } else {
+            const float xh = (v[u][j] - m[j]) * inv[j];
+            acc_a[j] += g[u][j];
+            acc_b[j] = fmaf(g[u][j], xh, acc_b[j]);
+          }
+        }
+      }
+    }
+    for (; r < r_end; r += step) {
       float v[VEC];
       VecT<VEC>::to(*reinterpret_cast<const V*>(x + r * C + c0), v);
       if (MODE == 0) {
@@ -130,7 +163,7 @@ __global__ void __launch_bounds__(kThreads)
         VecT<VEC>::to(*reinterpret_cast<const V*>(dy + r * C + c0), g);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float xh = (v[j] - s_mean[loc + j]) * s_inv[loc + j];
+          const float xh = (v[j] - m[j]) * inv[j];
           acc_a[j] += g[j];
           acc_b[j] = fmaf(g[j], xh, acc_b[j]);
         }
@@ -194,31 +227,70 @@ __global__ void bn_inv_std_kernel(const float* __restrict__ var, int C, float ep
   if (c < C) inv_std[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[c], eps)));
 }
 
+// Elementwise passes are row-tiled like the reductions: thread
+// (cg_local, r_off) of CTA (row block, channel chunk) owns channels
+// c0 .. c0+VEC-1 and rows r_off, r_off + rpi, ... of its row block, so its
+// per-channel constants sit in registers and each row costs one vector load
+// per input and one vector store, four rows in flight per thread.
+struct RowTile {
+  int c0;
+  int64_t r, r_end, step;
+  bool active;
+};
+
+__device__ __forceinline__ RowTile row_tile(int64_t rows, const ChunkGeom& geo) {
+  RowTile rt;
+  const int t = threadIdx.x;
+  const int cg_local = t % geo.cg;
+  const int r_off = t / geo.cg;
+  const int group = blockIdx.y * geo.cg + cg_local;
+  rt.active = r_off < geo.rpi && group < geo.groups;
+  rt.c0 = group * geo.vec;
+  const int64_t per_block = ceil_div(rows, gridDim.x);
+  const int64_t r_begin = (int64_t)blockIdx.x * per_block;
+  rt.r_end = r_begin + per_block < rows ? r_begin + per_block : rows;
+  rt.r = r_begin + r_off;
+  rt.step = geo.rpi;
+  return rt;
+}
+
 // y = gamma * ((x - mean) * inv_std) + beta (batchnorm_kernels.cl:77-80).
 template <int VEC>
 __global__ void __launch_bounds__(kThreads)
     bn_normalize_kernel(const float* __restrict__ x, const float* __restrict__ mean,
                         const float* __restrict__ inv_std, const float* __restrict__ gamma,
-                        const float* __restrict__ beta, float* __restrict__ y, int64_t total, int C) {
+                        const float* __restrict__ beta, float* __restrict__ y, int64_t rows, int C, ChunkGeom geo) {
   using V = typename VecT<VEC>::T;
-  const int64_t nv = total / VEC;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  int c0 = (int)((i * VEC) % C);
-  const int step = (int)((stride * VEC) % C);
-  for (; i < nv; i += stride, c0 = (c0 + step >= C) ? c0 + step - C : c0 + step) {
-    float v[VEC], o[VEC];
-    VecT<VEC>::to(reinterpret_cast<const V*>(x)[i], v);
+  RowTile rt = row_tile(rows, geo);
+  if (!rt.active) return;
+  float m[VEC], iv[VEC], g[VEC], b[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const int c = c0 + j;
-      const float xh = __fmul_rn(__fsub_rn(v[j], __ldg(mean + c)), __ldg(inv_std + c));
-      o[j] = __fadd_rn(__fmul_rn(__ldg(gamma + c), xh), __ldg(beta + c));
+  for (int j = 0; j < VEC; ++j) {
+    m[j] = mean[rt.c0 + j];
+    iv[j] = inv_std[rt.c0 + j];
+    g[j] = gamma[rt.c0 + j];
+    b[j] = beta[rt.c0 + j];
+  }
+  auto one = [&](const float* v, float* o) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) o[j] = __fadd_rn(__fmul_rn(g[j], __fmul_rn(__fsub_rn(v[j], m[j]), iv[j])), b[j]);
+  };
+  constexpr int U = 4;
+  for (; rt.r + (U - 1) * rt.step < rt.r_end; rt.r += U * rt.step) {
+    float v[U][VEC], o[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) VecT<VEC>::to(*reinterpret_cast<const V*>(x + (rt.r + u * rt.step) * C + rt.c0), v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      one(v[u], o[u]);
+      VecT<VEC>::from(o[u], reinterpret_cast<V*>(y + (rt.r + u * rt.step) * C + rt.c0));
     }
-    if (VEC == 4)
-      reinterpret_cast<float4*>(y)[i] = make_float4(o[0], o[1], o[2], o[3]);
-    else
-      y[i] = o[0];
+  }
+  for (; rt.r < rt.r_end; rt.r += rt.step) {
+    float v[VEC], o[VEC];
+    VecT<VEC>::to(*reinterpret_cast<const V*>(x + rt.r * C + rt.c0), v);
+    one(v, o);
+    VecT<VEC>::from(o, reinterpret_cast<V*>(y + rt.r * C + rt.c0));
   }
 }
 
@@ -258,31 +330,62 @@ __global__ void __launch_bounds__(kThreads)
     bn_grad_dx_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
                       const float* __restrict__ inv_std, const float* __restrict__ k1,
                       const float* __restrict__ grad_beta, const float* __restrict__ grad_gamma,
-                      float* __restrict__ dx, int64_t total, int C, float nhw_f) {
+                      float* __restrict__ dx, int64_t rows, int C, float nhw_f, ChunkGeom geo) {
   using V = typename VecT<VEC>::T;
-  const int64_t nv = total / VEC;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  int c0 = (int)((i * VEC) % C);
-  const int step = (int)((stride * VEC) % C);
-  for (; i < nv; i += stride, c0 = (c0 + step >= C) ? c0 + step - C : c0 + step) {
-    float vx[VEC], vg[VEC], o[VEC];
-    VecT<VEC>::to(reinterpret_cast<const V*>(x)[i], vx);
-    VecT<VEC>::to(reinterpret_cast<const V*>(dy)[i], vg);
+  RowTile rt = row_tile(rows, geo);
+  if (!rt.active) return;
+  float m[VEC], iv[VEC], kk[VEC], db[VEC], dg[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    m[j] = mean[rt.c0 + j];
+    iv[j] = inv_std[rt.c0 + j];
+    kk[j] = k1[rt.c0 + j];
+    db[j] = grad_beta[rt.c0 + j];
+    dg[j] = grad_gamma[rt.c0 + j];
+  }
+  auto one = [&](const float* vx, const float* vg, float* o) {
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
-      const int c = c0 + j;
-      const float xh = __fmul_rn(__fsub_rn(vx[j], __ldg(mean + c)), __ldg(inv_std + c));
+      const float xh = __fmul_rn(__fsub_rn(vx[j], m[j]), iv[j]);
       float t = __fmul_rn(nhw_f, vg[j]);
-      t = __fsub_rn(t, __ldg(grad_beta + c));
-      t = __fsub_rn(t, __fmul_rn(xh, __ldg(grad_gamma + c)));
-      o[j] = __fmul_rn(__ldg(k1 + c), t);
+      t = __fsub_rn(t, db[j]);
+      t = __fsub_rn(t, __fmul_rn(xh, dg[j]));
+      o[j] = __fmul_rn(kk[j], t);
     }
-    if (VEC == 4)
-      reinterpret_cast<float4*>(dx)[i] = make_float4(o[0], o[1], o[2], o[3]);
-    else
-      dx[i] = o[0];
+  };
+  constexpr int U = 4;
+  for (; rt.r + (U - 1) * rt.step < rt.r_end; rt.r += U * rt.step) {
+    float vx[U][VEC], vg[U][VEC], o[VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t off = (rt.r + u * rt.step) * C + rt.c0;
+      VecT<VEC>::to(*reinterpret_cast<const V*>(x + off), vx[u]);
+      VecT<VEC>::to(*reinterpret_cast<const V*>(dy + off), vg[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      one(vx[u], vg[u], o);
+      VecT<VEC>::from(o, reinterpret_cast<V*>(dx + (rt.r + u * rt.step) * C + rt.c0));
+    }
   }
+  for (; rt.r < rt.r_end; rt.r += rt.step) {
+    float vx[VEC], vg[VEC], o[VEC];
+    const int64_t off = rt.r * C + rt.c0;
+    VecT<VEC>::to(*reinterpret_cast<const V*>(x + off), vx);
+    VecT<VEC>::to(*reinterpret_cast<const V*>(dy + off), vg);
+    one(vx, vg, o);
+    VecT<VEC>::from(o, reinterpret_cast<V*>(dx + off));
+  }
+}
+
+// CTAs for an elementwise row-tiled pass: about 8 per SM, at least 4 rows per
+// thread.
+int ew_row_blocks(int64_t rows, const ChunkGeom& geo, int sm_count) {
+  int64_t want = (int64_t)sm_count * 8 / geo.chunks;
+  if (want < 1) want = 1;
+  int64_t cap = ceil_div(rows, (int64_t)geo.rpi * 4);
+  if (cap < 1) cap = 1;
+  return (int)(want < cap ? want : cap);
 }
 
 int validate_nhwc(const int64_t* s, const char* what) {
@@ -315,13 +418,15 @@ int launch_partials(cudaStream_t s, int mode, const float* x, const float* dy, c
 
 int launch_normalize(cudaStream_t s, const float* x, const float* mean, const float* inv, const float* gamma,
                      const float* beta, float* y, int64_t total, int C, bool vec_ok) {
-  if (vec_ok) {
-    bn_normalize_kernel<4><<<grid_for(total / 4, kThreads, 8), kThreads, 0, s>>>(x, mean, inv, gamma, beta, y,
-                                                                               total, C);
-  } else {
-    bn_normalize_kernel<1><<<grid_for(total, kThreads, 8), kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, total,
-                                                                           C);
-  }
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int64_t rows = total / C;
+  dim3 grid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
+  if (vec_ok)
+    bn_normalize_kernel<4><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+  else
+    bn_normalize_kernel<1><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
   return check_launch(s, "bn_normalize");
 }
 
@@ -418,12 +523,13 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t gr
   B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
   if (total == 0) return B2_OK;
   const float nhw_f = (float)(int)rows;
+  dim3 egrid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
   if (vec_ok) {
-    bn_grad_dx_kernel<4><<<grid_for(total / 4, kThreads, 8), kThreads, 0, s>>>(
-        grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x, total, (int)C, nhw_f);
+    bn_grad_dx_kernel<4><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x,
+                                                   rows, (int)C, nhw_f, geo);
   } else {
-    bn_grad_dx_kernel<1><<<grid_for(total, kThreads, 8), kThreads, 0, s>>>(
-        grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x, total, (int)C, nhw_f);
+    bn_grad_dx_kernel<1><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x,
+                                                   rows, (int)C, nhw_f, geo);
   }
   return check_launch(s, "bn_backward_dx");
 }

@@ -52,12 +52,13 @@ __global__ void __launch_bounds__(kThreads) dw_fwd_vec4_kernel(const float* __re
   const int64_t total = (int64_t)a.N * a.Ho * a.Wo * cg;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
-    const int c = (int)(g % cg) * 4;
-    int64_t p = g / cg;
-    const int wo = (int)(p % a.Wo);
-    p /= a.Wo;
-    const int ho = (int)(p % a.Ho);
-    const int n = (int)(p / a.Ho);
+    uint32_t p = (uint32_t)g / (uint32_t)cg;  // element counts < 2^31 (checked on the host)
+    const int c = (int)((uint32_t)g - p * (uint32_t)cg) * 4;
+    uint32_t q = p / (uint32_t)a.Wo;
+    const int wo = (int)(p - q * (uint32_t)a.Wo);
+    const uint32_t n32 = q / (uint32_t)a.Ho;
+    const int ho = (int)(q - n32 * (uint32_t)a.Ho);
+    const int n = (int)n32;
     const int hi0 = ho * a.sH - a.pH, wi0 = wo * a.sW - a.pW;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int kh = 0; kh < a.kH; ++kh) {
@@ -117,23 +118,24 @@ __global__ void __launch_bounds__(kThreads) dw_dgrad_vec4_kernel(const float* __
   const int64_t total = (int64_t)a.N * a.H * a.W * cg;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
-    const int c = (int)(g % cg) * 4;
-    int64_t p = g / cg;
-    const int wi = (int)(p % a.W);
-    p /= a.W;
-    const int hi = (int)(p % a.H);
-    const int n = (int)(p / a.H);
+    uint32_t p = (uint32_t)g / (uint32_t)cg;  // element counts < 2^31 (checked on the host)
+    const int c = (int)((uint32_t)g - p * (uint32_t)cg) * 4;
+    uint32_t q = p / (uint32_t)a.W;
+    const int wi = (int)(p - q * (uint32_t)a.W);
+    const uint32_t n32 = q / (uint32_t)a.H;
+    const int hi = (int)(q - n32 * (uint32_t)a.H);
+    const int n = (int)n32;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int kh = 0; kh < a.kH; ++kh) {
       const int hn = hi + a.pH - kh;
-      if (hn < 0 || hn % a.sH != 0) continue;
+      if (hn < 0) continue;
       const int ho = hn / a.sH;
-      if (ho >= a.Ho) continue;
+      if (ho * a.sH != hn || ho >= a.Ho) continue;
       for (int kw = 0; kw < a.kW; ++kw) {
         const int wn = wi + a.pW - kw;
-        if (wn < 0 || wn % a.sW != 0) continue;
+        if (wn < 0) continue;
         const int wo = wn / a.sW;
-        if (wo >= a.Wo) continue;
+        if (wo * a.sW != wn || wo >= a.Wo) continue;
         const float4 gv =
             __ldg(reinterpret_cast<const float4*>(dy + ((int64_t)(n * a.Ho + ho) * a.Wo + wo) * a.C + c));
         const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)(kh * a.kW + kw) * a.C + c));
@@ -209,10 +211,11 @@ __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_vec4_kernel(const f
 
   if (active) {
     for (int64_t p = p_begin + lane; p < p_end; p += lanes) {
-      const int wo = (int)(p % a.Wo);
-      const int64_t q = p / a.Wo;
-      const int ho = (int)(q % a.Ho);
-      const int n = (int)(q / a.Ho);
+      const uint32_t q = (uint32_t)p / (uint32_t)a.Wo;  // pixel counts < 2^31 (checked on the host)
+      const int wo = (int)((uint32_t)p - q * (uint32_t)a.Wo);
+      const uint32_t n32 = q / (uint32_t)a.Ho;
+      const int ho = (int)(q - n32 * (uint32_t)a.Ho);
+      const int n = (int)n32;
       const float4 gv = __ldg(reinterpret_cast<const float4*>(dy + p * a.C + c));
       const int hi0 = ho * a.sH - a.pH, wi0 = wo * a.sW - a.pW;
 #pragma unroll

@@ -374,33 +374,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
       const TileCoord tc = tile_coord(p, bn, t);
       const auto ca0 = p.a.row(tc.m0 + rsub);
       const auto ca1 = p.a.row(tc.m0 + rsub + 64);
-      typename decltype(p.b)::Ctx cb[4];
+      typename decltype(p.b)::Ctx cb[3];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cb[j] = p.b.row(tc.n0 + rsub + 64 * j);
+      for (int j = 0; j < 3; ++j) cb[j] = p.b.row(tc.n0 + rsub + 64 * j);
       for (int kb = 0; kb < tc.nkb; ++kb, ++stage_cnt) {
         const int s = (int)(stage_cnt % (uint32_t)stages);
         const uint32_t round = stage_cnt / (uint32_t)stages;
+        // Issue every load of this k-block (2 A pieces, up to 3 B pieces)
+        // before waiting for the stage or storing: one memory round trip per
+        // k-block, overlapped with the wait for the slot.
+        const int64_t k = tc.k_begin + (int64_t)kb * BK + q * kUnit;
+        float va0[kUnit], va1[kUnit], vb[3][kUnit];
+        p.a.load8(ca0, k, tc.k_end, va0);
+        p.a.load8(ca1, k, tc.k_end, va1);
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const int r = rsub + 64 * j;
+          if (r < bn) {
+            if (tc.n0 + r < p.N) p.b.load8(cb[j], k, tc.k_end, vb[j]); else zero_unit(vb[j]);
+          }
+        }
         if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) break;
         uint8_t* st = smem + (size_t)s * stage_bytes;
-        const int64_t k = tc.k_begin + (int64_t)kb * BK + q * kUnit;
-        float v0[kUnit], v1[kUnit];
-        p.a.load8(ca0, k, tc.k_end, v0);
-        p.a.load8(ca1, k, tc.k_end, v1);
-        store_unit_split(st, st + a_bytes, rsub, q, v0);
-        store_unit_split(st, st + a_bytes, rsub + 64, q, v1);
+        store_unit_split(st, st + a_bytes, rsub, q, va0);
+        store_unit_split(st, st + a_bytes, rsub + 64, q, va1);
         uint8_t* bhi = st + 2 * a_bytes;
         uint8_t* blo = bhi + b_bytes;
 #pragma unroll
-        for (int j = 0; j < 4; j += 2) {
-          const int r0 = rsub + 64 * j, r1 = r0 + 64;
-          if (r0 < bn) {
-            if (tc.n0 + r0 < p.N) p.b.load8(cb[j], k, tc.k_end, v0); else zero_unit(v0);
-          }
-          if (r1 < bn) {
-            if (tc.n0 + r1 < p.N) p.b.load8(cb[j + 1], k, tc.k_end, v1); else zero_unit(v1);
-          }
-          if (r0 < bn) store_unit_split(bhi, blo, r0, q, v0);
-          if (r1 < bn) store_unit_split(bhi, blo, r1, q, v1);
+        for (int j = 0; j < 3; ++j) {
+          const int r = rsub + 64 * j;
+          if (r < bn) store_unit_split(bhi, blo, r, q, vb[j]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(&full[s]);

@@ -75,12 +75,13 @@ __global__ void __launch_bounds__(kThreads) up_fwd_kernel(const float* __restric
   const int64_t total = (int64_t)a.N * a.Ho * a.Wo * cg;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
-    const int c = (int)(g % cg) * VEC;
-    int64_t p = g / cg;
-    const int ow = (int)(p % a.Wo);
-    p /= a.Wo;
-    const int oh = (int)(p % a.Ho);
-    const int n = (int)(p / a.Ho);
+    const uint32_t p = (uint32_t)g / (uint32_t)cg;  // element counts < 2^31 (checked on the host)
+    const int c = (int)((uint32_t)g - p * (uint32_t)cg) * VEC;
+    const uint32_t q = p / (uint32_t)a.Wo;
+    const int ow = (int)(p - q * (uint32_t)a.Wo);
+    const uint32_t n32 = q / (uint32_t)a.Ho;
+    const int oh = (int)(q - n32 * (uint32_t)a.Ho);
+    const int n = (int)n32;
     const Coord ch = up_coord(oh, a.H, a.Ho);
     const Coord cw = up_coord(ow, a.W, a.Wo);
     const float* base = x + (int64_t)n * a.H * a.W * a.C + c;
@@ -116,12 +117,13 @@ __global__ void __launch_bounds__(kThreads) up_bwd_kernel(const float* __restric
   const int64_t total = (int64_t)a.N * a.H * a.W * cg;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
-    const int c = (int)(g % cg) * VEC;
-    int64_t p = g / cg;
-    const int iw = (int)(p % a.W);
-    p /= a.W;
-    const int ih = (int)(p % a.H);
-    const int n = (int)(p / a.H);
+    const uint32_t p = (uint32_t)g / (uint32_t)cg;  // element counts < 2^31 (checked on the host)
+    const int c = (int)((uint32_t)g - p * (uint32_t)cg) * VEC;
+    const uint32_t q = p / (uint32_t)a.W;
+    const int iw = (int)(p - q * (uint32_t)a.W);
+    const uint32_t n32 = q / (uint32_t)a.H;
+    const int ih = (int)(q - n32 * (uint32_t)a.H);
+    const int n = (int)n32;
     // Every output row whose corners can reach input row ih lies in
     // [(ih-1)*sy - 1, (ih+2)*sy] (the exact test below decides).
     const int oh_lo = max(0, (ih - 1) * sy - 1), oh_hi = min(a.Ho - 1, (ih + 2) * sy);

@@ -168,3 +168,50 @@ def summarize(rows) -> dict:
     return out
 
 
+
+
+def _cli() -> int:
+    """Replay one op of the README network's training step, e.g. for ncu:
+
+        PYTHONPATH=opencl-tensorflow_b200 python -m opencl_tf.profile --op conv2d --call 0 --reps 3
+
+    records one step at --batch (default 256), then runs the --call-th call of
+    --op (in step order) --reps times after one warm-up run; --list prints
+    the step's op calls with their per-op times.
+    """
+    import argparse
+    import sys
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="conv2d_backprop_filter")
+    ap.add_argument("--call", type=int, default=0)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--list", action="store_true")
+    a = ap.parse_args()
+    from .model import build_model
+    from .train import mse
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    model = build_model(device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.rand(a.batch, 64, 64, 3, device=dev, generator=g)
+    t = torch.rand(a.batch, 8, 8, 8, device=dev, generator=g)
+    _, log = record_step(lambda: mse(model(x, training=True), t).backward())
+    if a.list:
+        for r, (name, *_rest) in zip(time_ops(log), log):
+            print(f"{name:36s} {r['ms']:8.4f} ms  {r['achieved']:9.1f} {r['unit']:8s} frac {r['frac']:.3f}")
+        return 0
+    calls = [e for e in log if e[0] == a.op]
+    if a.call >= len(calls):
+        print(f"op {a.op} has {len(calls)} calls in the step", file=sys.stderr)
+        return 2
+    _, orig, args, kw, _ = calls[a.call]
+    for _ in range(1 + a.reps):
+        orig(*args, **kw)
+    torch.cuda.synchronize()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_cli())
