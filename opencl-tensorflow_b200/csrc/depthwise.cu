@@ -126,16 +126,19 @@ __global__ void __launch_bounds__(kThreads) dw_dgrad_vec4_kernel(const float* __
     const int hi = (int)(q - n32 * (uint32_t)a.H);
     const int n = (int)n32;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int kh = 0; kh < a.kH; ++kh) {
+    // Only taps with (hi + pH - kh) % sH == 0 reach this pixel: start at the
+    // first such kh and step by the stride (ascending, as the reference).
+    const int kh0 = (hi + a.pH) % a.sH, kw0 = (wi + a.pW) % a.sW;
+    for (int kh = kh0; kh < a.kH; kh += a.sH) {
       const int hn = hi + a.pH - kh;
-      if (hn < 0) continue;
+      if (hn < 0) break;
       const int ho = hn / a.sH;
-      if (ho * a.sH != hn || ho >= a.Ho) continue;
-      for (int kw = 0; kw < a.kW; ++kw) {
+      if (ho >= a.Ho) continue;
+      for (int kw = kw0; kw < a.kW; kw += a.sW) {
         const int wn = wi + a.pW - kw;
-        if (wn < 0) continue;
+        if (wn < 0) break;
         const int wo = wn / a.sW;
-        if (wo * a.sW != wn || wo >= a.Wo) continue;
+        if (wo >= a.Wo) continue;
         const float4 gv =
             __ldg(reinterpret_cast<const float4*>(dy + ((int64_t)(n * a.Ho + ho) * a.Wo + wo) * a.C + c));
         const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)(kh * a.kW + kw) * a.C + c));
@@ -210,6 +213,12 @@ __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_vec4_kernel(const f
   for (int k = 0; k < KMAX; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   if (active) {
+    int tdh[KMAX], tdw[KMAX];  // tap offsets, divided once per thread
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      tdh[k] = k / a.kW;
+      tdw[k] = k - tdh[k] * a.kW;
+    }
     for (int64_t p = p_begin + lane; p < p_end; p += lanes) {
       const uint32_t q = (uint32_t)p / (uint32_t)a.Wo;  // pixel counts < 2^31 (checked on the host)
       const int wo = (int)((uint32_t)p - q * (uint32_t)a.Wo);
@@ -221,7 +230,7 @@ __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_vec4_kernel(const f
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k < taps) {
-          const int hi = hi0 + k / a.kW, wi = wi0 + k % a.kW;
+          const int hi = hi0 + tdh[k], wi = wi0 + tdw[k];
           if ((unsigned)hi < (unsigned)a.H && (unsigned)wi < (unsigned)a.W) {
             const float4 xv =
                 __ldg(reinterpret_cast<const float4*>(x + ((int64_t)(n * a.H + hi) * a.W + wi) * a.C + c));
@@ -420,9 +429,9 @@ int b2_depthwise_conv2d_backprop_filter(b2_stream_t stream, const float* input, 
     const int cg_total = (int)(g.Ci / 4);
     const int cg_per_cta = cg_total < kThreads ? cg_total : kThreads;
     const int chunks = (int)ceil_div(cg_total, cg_per_cta);
-    int64_t want = (int64_t)d->sm_count * 4 / chunks;
+    int64_t want = (int64_t)d->sm_count * 8 / chunks;
     if (want < 1) want = 1;
-    int64_t cap = ceil_div(pixels, 64);
+    int64_t cap = ceil_div(pixels, 32);
     blocks = (int)(want < cap ? want : cap);
     const int64_t ppb = ceil_div(pixels, blocks);
     blocks = (int)ceil_div(pixels, ppb);

@@ -330,7 +330,16 @@ __global__ void dense_bias_grad_kernel(const float* __restrict__ dy, int64_t bat
   const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= out_f) return;
   float acc = 0.0f;
-  for (int64_t n = 0; n < batch; ++n) acc = __fadd_rn(acc, __ldg(dy + n * out_f + o));
+  constexpr int kAhead = 16;  // loads issued ahead of the in-order adds
+  int64_t n = 0;
+  for (; n + kAhead <= batch; n += kAhead) {
+    float v[kAhead];
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) v[i] = __ldg(dy + (n + i) * out_f + o);
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) acc = __fadd_rn(acc, v[i]);
+  }
+  for (; n < batch; ++n) acc = __fadd_rn(acc, __ldg(dy + n * out_f + o));
   db[o] = acc;
 }
 
@@ -505,7 +514,7 @@ int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dense_bias_grad_kernel<<<(unsigned)ceil_div(out_f, 128), 128, 0, s>>>(grad_y, batch, out_f, grad_b);
+  dense_bias_grad_kernel<<<(unsigned)ceil_div(out_f, 32), 32, 0, s>>>(grad_y, batch, out_f, grad_b);
   return check_launch(s, "dense_backprop_bias");
 }
 

@@ -132,14 +132,38 @@ __global__ void __launch_bounds__(kThreads) up_bwd_kernel(const float* __restric
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
     const float* gbase = dy + (int64_t)n * a.Ho * a.Wo * a.C + c;
+    // The output columns that reach input column iw, computed once per
+    // thread: bit 0 = lower corner is iw, bit 1 = upper corner is iw.
+    constexpr int kMaxCols = 64;
+    uint8_t col_hit[kMaxCols];
+    float col_frac[kMaxCols];
+    const int ncols = ow_hi - ow_lo + 1;
+    const bool cached = ncols <= kMaxCols;
+    if (cached) {
+      for (int j = 0; j < ncols; ++j) {
+        const Coord cw = up_coord(ow_lo + j, a.W, a.Wo);
+        col_hit[j] = (uint8_t)((cw.lo == iw ? 1 : 0) | (cw.hi == iw ? 2 : 0));
+        col_frac[j] = cw.frac;
+      }
+    }
     for (int oh = oh_lo; oh <= oh_hi; ++oh) {
       const Coord ch = up_coord(oh, a.H, a.Ho);
       const bool h0 = ch.lo == ih, h1 = ch.hi == ih;
       if (!h0 && !h1) continue;
       const float a_h = __fsub_rn(1.0f, ch.frac);
       for (int ow = ow_lo; ow <= ow_hi; ++ow) {
-        const Coord cw = up_coord(ow, a.W, a.Wo);
-        const bool w0 = cw.lo == iw, w1 = cw.hi == iw;
+        Coord cw;
+        bool w0, w1;
+        if (cached) {
+          const int hit = col_hit[ow - ow_lo];
+          w0 = hit & 1;
+          w1 = hit & 2;
+          cw.frac = col_frac[ow - ow_lo];
+        } else {
+          cw = up_coord(ow, a.W, a.Wo);
+          w0 = cw.lo == iw;
+          w1 = cw.hi == iw;
+        }
         if (!w0 && !w1) continue;
         float gv[VEC];
         const T t = *reinterpret_cast<const T*>(gbase + ((int64_t)oh * a.Wo + ow) * a.C);
