@@ -18,8 +18,14 @@
 // the output tiles alone cannot fill the GPU (filter grads, the dense forward
 // at small batch) K is split across CTAs; partials are summed in split order
 // by a second kernel, so every result is deterministic.
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <type_traits>
+
 #include "conv_common.cuh"
 #include "tc_gemm.cuh"
+#include "tma_gemm.cuh"
 
 namespace b2 {
 namespace tc {
@@ -301,12 +307,162 @@ struct ConvWgradA {
   }
 };
 
+// ------------------------------------------------- TMA engine (host side)
+
+// A plain matrix operand: op(r, k) = p[r*ld + k] (K-major) or p[k*ld + r].
+struct MatOperand {
+  const float* p;
+  int64_t rows, ld;
+  bool k_major;
+};
+
+inline MatOperand mat_of(const KContig& v) { return MatOperand{v.p, v.rows, v.ld, true}; }
+inline MatOperand mat_of(const MNMajor& v) { return MatOperand{v.p, v.rows, v.ld, false}; }
+template <class V>
+struct is_mat_view : std::false_type {};
+template <>
+struct is_mat_view<KContig> : std::true_type {};
+template <>
+struct is_mat_view<MNMajor> : std::true_type {};
+
+// cuTensorMapEncodeTiled, fetched once through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// The TMA engine is on unless B2_TMA_GEMM=0 (then every contraction runs on
+// the register-fed engine).
+bool tma_engine_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_TMA_GEMM");
+    return !(e && e[0] == '0');
+  }();
+  return on && tensor_map_encoder() != nullptr;
+}
+
+constexpr int64_t kI32 = 2147483647;
+
+bool tma_operand_ok(const MatOperand& o, int64_t K) {
+  return aligned16(o.p) && o.ld % 4 == 0 && o.rows <= kI32 && K <= kI32 && o.ld <= kI32;
+}
+
+int encode_map(CUtensorMap* m, const float* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+               const cuuint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const CUresult r = tensor_map_encoder()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
+                                          const_cast<float*>(base), dims, strides, box, elem,
+                                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(B2_ERR_INTERNAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B2_OK;
+}
+
+// Operand map: K-major -> dims {K, rows}, box {32, box_rows}, 128-byte
+// swizzle; MN-major -> dims {rows, K}, box {32, 32}, 128-byte swizzle of
+// 32-byte atoms (what MN-major tf32 UMMA reads).
+int encode_operand(CUtensorMap* m, const MatOperand& o, int64_t K, int box_rows) {
+  const cuuint64_t strides[1] = {(cuuint64_t)o.ld * 4};
+  if (o.k_major) {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)o.rows};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    return encode_map(m, o.p, 2, dims, strides, box);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)o.rows, (cuuint64_t)K};
+  const cuuint32_t box[2] = {32, (cuuint32_t)BK};
+  return encode_map(m, o.p, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
+// N tile of the TMA engine: a multiple of 32 (whole 32-column output blocks),
+// at most 128, balanced over the N tiles.
+int tma_bn(int64_t N) {
+  if (N <= kTmaMaxBN) return (int)(ceil_div(N < 32 ? 32 : N, 32) * 32);
+  const int64_t tiles = ceil_div(N, kTmaMaxBN);
+  return (int)(ceil_div(ceil_div(N, tiles), 32) * 32);
+}
+
+int tma_stages(int bn, int max_smem) {
+  const TmaSmem fixed = tma_smem_plan(bn, 0);
+  int st = (int)((max_smem - (int)fixed.total) / (int)fixed.stage_bytes);
+  if (st > kTmaMaxStages) st = kTmaMaxStages;
+  return st;
+}
+
+template <bool kAK, bool kBK>
+int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
+               int stages, int grid, cudaStream_t s, const char* name) {
+  const TmaSmem plan = tma_smem_plan(prob.bn, stages);
+  static int configured_bytes = 0;  // per instantiation
+  if ((int)plan.total > configured_bytes) {
+    B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<kAK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)plan.total));
+    configured_bytes = (int)plan.total;
+  }
+  tma_gemm_kernel<kAK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, stages);
+  return check_launch(s, name);
+}
+
+int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N, int64_t K, float* out,
+                 const float* bias, cudaStream_t s, const char* name, int min_kb_per_split) {
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  const int bn = tma_bn(N);
+  const int stages = tma_stages(bn, d->max_smem_optin);
+  if (stages < 2) return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
+  const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
+  int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);
+  int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
+  if (kps < BK) kps = BK;
+  splits = (int)ceil_div(K, kps);
+  TmaProblem prob{M, N, K, kps, splits, bn, bias, false};
+  CUtensorMap ma, mb, md;
+  B2_RETURN_IF_ERROR(encode_operand(&ma, a, K, BM));
+  B2_RETURN_IF_ERROR(encode_operand(&mb, b, K, bn));
+  const cuuint32_t obox[3] = {32, 32, 1};
+  Scratch part;
+  if (splits == 1) {
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)N * 4};
+    B2_RETURN_IF_ERROR(encode_map(&md, out, 2, dims, strides, obox));
+  } else {
+    B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)splits * M * N, s));
+    const cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)splits};
+    const cuuint64_t strides[2] = {(cuuint64_t)N * 4, (cuuint64_t)(M * N * 4)};
+    B2_RETURN_IF_ERROR(encode_map(&md, part.as<float>(), 3, dims, strides, obox));
+    prob.partial = true;
+    prob.bias = nullptr;
+  }
+  const int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
+  int rc;
+  if (a.k_major && b.k_major) rc = launch_tma<true, true>(ma, mb, md, prob, stages, grid, s, name);
+  else if (a.k_major) rc = launch_tma<true, false>(ma, mb, md, prob, stages, grid, s, name);
+  else if (b.k_major) rc = launch_tma<false, true>(ma, mb, md, prob, stages, grid, s, name);
+  else rc = launch_tma<false, false>(ma, mb, md, prob, stages, grid, s, name);
+  B2_RETURN_IF_ERROR(rc);
+  if (splits == 1) return B2_OK;
+  splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  return check_launch(s, "splitk_reduce");
+}
+
 template <class AV, class BV>
 int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* out, const float* bias,
              cudaStream_t s, const char* name, int min_kb_per_split = 4) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   if (M == 0 || N == 0) return B2_OK;
+  if constexpr (is_mat_view<AV>::value && is_mat_view<BV>::value) {
+    const MatOperand ma = mat_of(a), mb = mat_of(b);
+    if (K > 0 && tma_engine_enabled() && tma_operand_ok(ma, K) && tma_operand_ok(mb, K) && aligned16(out) &&
+        N % 4 == 0 && M <= kI32 && N <= kI32)
+      return run_tma_gemm(ma, mb, M, N, K, out, bias, s, name, min_kb_per_split);
+  }
   const int bn = choose_bn(N);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
   int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);

@@ -25,7 +25,9 @@ def test_dense_forward_basic(otf, port):
 
 
 @pytest.mark.parametrize("batch,in_f,out_f", [(1, 1, 1), (8, 32, 64), (16, 64, 32), (3, 128, 10), (256, 1152, 128),
-                                              (130, 300, 270), (5, 0, 3), (2, 4097, 17)])
+                                              (130, 300, 270), (5, 0, 3), (2, 4097, 17),
+                                              # ragged sizes with 16-byte-aligned rows (TMA-fed engine)
+                                              (130, 300, 276), (3, 4100, 20), (300, 20, 36), (257, 2052, 132)])
 def test_dense_all_ops(otf, port, batch, in_f, out_f):
     rng = np.random.default_rng(42)
     x = rng.standard_normal((batch, in_f)).astype(np.float32)
