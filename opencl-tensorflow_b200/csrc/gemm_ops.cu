@@ -366,9 +366,10 @@ int encode_map(CUtensorMap* m, const float* base, int rank, const cuuint64_t* di
 }
 
 // Operand map: K-major -> dims {K, rows}, box {32, box_rows}, 128-byte
-// swizzle; MN-major -> dims {rows, K}, box {32, 32}, 128-byte swizzle of
-// 32-byte atoms (what MN-major tf32 UMMA reads).
-int encode_operand(CUtensorMap* m, const MatOperand& o, int64_t K, int box_rows) {
+// swizzle; MN-major -> dims {rows, K}, box {32, 32}, with `mn_swizzle` (B:
+// the 128-byte swizzle of 32-byte atoms that MN-major tf32 UMMA reads; A:
+// none, the converters read it).
+int encode_operand(CUtensorMap* m, const MatOperand& o, int64_t K, int box_rows, CUtensorMapSwizzle mn_swizzle) {
   const cuuint64_t strides[1] = {(cuuint64_t)o.ld * 4};
   if (o.k_major) {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)o.rows};
@@ -377,7 +378,7 @@ int encode_operand(CUtensorMap* m, const MatOperand& o, int64_t K, int box_rows)
   }
   const cuuint64_t dims[2] = {(cuuint64_t)o.rows, (cuuint64_t)K};
   const cuuint32_t box[2] = {32, (cuuint32_t)BK};
-  return encode_map(m, o.p, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  return encode_map(m, o.p, 2, dims, strides, box, mn_swizzle);
 }
 
 // N tile of the TMA engine: a multiple of 32 (whole 32-column output blocks),
@@ -388,9 +389,12 @@ int tma_bn(int64_t N) {
   return (int)(ceil_div(ceil_div(N, tiles), 32) * 32);
 }
 
-int tma_stages(int bn, int max_smem) {
+// Stages: limited by shared memory and by the TMEM columns left for A slots.
+int tma_stages(int bn, bool use_s, int max_smem) {
   const TmaSmem fixed = tma_smem_plan(bn, 0);
   int st = (int)((max_smem - (int)fixed.total) / (int)fixed.stage_bytes);
+  const int by_tmem = (int)((kTmemCols - tma_acc_cols(bn, use_s)) / kASlotCols);
+  if (st > by_tmem) st = by_tmem;
   if (st > kTmaMaxStages) st = kTmaMaxStages;
   return st;
 }
@@ -414,17 +418,18 @@ int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N,
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   const int bn = tma_bn(N);
-  const int stages = tma_stages(bn, d->max_smem_optin);
-  if (stages < 2) return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
   int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);
   int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
   if (kps < BK) kps = BK;
   splits = (int)ceil_div(K, kps);
-  TmaProblem prob{M, N, K, kps, splits, bn, bias, false};
+  const bool use_s = kps > (int64_t)kChunkKB * BK;
+  const int stages = tma_stages(bn, use_s, d->max_smem_optin);
+  if (stages < 2) return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
+  TmaProblem prob{M, N, K, kps, splits, bn, bias, false, use_s};
   CUtensorMap ma, mb, md;
-  B2_RETURN_IF_ERROR(encode_operand(&ma, a, K, BM));
-  B2_RETURN_IF_ERROR(encode_operand(&mb, b, K, bn));
+  B2_RETURN_IF_ERROR(encode_operand(&ma, a, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
+  B2_RETURN_IF_ERROR(encode_operand(&mb, b, K, bn, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
   const cuuint32_t obox[3] = {32, 32, 1};
   Scratch part;
   if (splits == 1) {

@@ -2,40 +2,51 @@
 // for contractions whose operands are plain row-major matrices (Dense forward
 // and backward, 1x1 / stride-1 / unpadded Conv2D forward and gradients).
 //
-// Each operand is K-major (op(r, k) = p[r*ld + k]) or MN-major
-// (op(r, k) = p[k*ld + r]); both are loaded as 128-byte-swizzled tiles that
-// the tensor core reads directly in that major-ness, so no thread ever
-// gathers or transposes operand data:
+// D[M,N] = sum_k A[m,k] B[k,n].  Each operand is K-major (op(r, k) =
+// p[r*ld + k]) or MN-major (op(r, k) = p[k*ld + r]).  Per 32-wide k-block:
 //
-//   K-major  tile [R rows][32 k]          one TMA box {32, R}; UMMA K-major
-//            SWIZZLE_128B, SBO = 1024 B (8-row groups), k step = +32 B.
-//   MN-major tile [R/32][32 k][32 rows]   R/32 TMA boxes {32, 32} with the
-//            128-byte swizzle of 32-byte atoms (the only MN-major smem
-//            layout tf32 UMMA accepts); UMMA MN-major SWIZZLE_128B_BASE32B,
-//            LBO = 4096 B (32-row blocks), SBO = 512 B (4-k groups),
-//            k step = +1024 B.
+//   A  TMA loads the raw fp32 tile (K-major: one box {32, 128} with the
+//      128-byte swizzle, so the converters' row reads are conflict-free;
+//      MN-major: four boxes {32 rows, 32 k}, unswizzled).  The converter
+//      warps split each element x -> hi = tf32(x), lo = tf32(x - hi) and
+//      write both into a tensor-memory slot (128 lanes = rows, 32 + 32
+//      columns), where the MMA reads A.  A never returns to shared memory,
+//      so the three MMAs of a k step read only B from it.
+//   B  TMA loads the tile in the layout UMMA reads in place (K-major: box
+//      {32, BN}, 128-byte swizzle, SBO = 1024 B, k step +32 B; MN-major: BN/32
+//      boxes {32, 32} with the 128-byte swizzle of 32-byte atoms, the only
+//      MN-major smem layout tf32 UMMA accepts, LBO = 4096 B, SBO = 512 B,
+//      k step +1024 B); the converters split it in place (hi where x was, lo
+//      at the same offset of the stage's lo tile, so the swizzle carries over).
 //
 // Out-of-range rows and k are zero-filled by the TMA unit.  One CTA per SM
-// loops over output tiles 128 x BN (BN a multiple of 32, <= 128) and split-K
+// loops over output tiles 128 x BN (BN a multiple of 32, <= 96) and split-K
 // slices, with four warp roles:
 //
 //   warp 0       lane 0 waits for a free stage (EMPTY), posts the stage's
-//                byte count on RAW_FULL and issues the TMA loads of A and B.
-//   warp 1       allocates TMEM (chunk accumulators P0, P1 and running sum
-//                S); lane 0 waits CONV_FULL and issues, per 8-wide k step,
-//                P += Alo*Bhi + Ahi*Blo + Ahi*Bhi, commits EMPTY per stage and
-//                CHUNK_FULL per chunk (at most kChunkKB k-blocks).
-//   warps 2-9    converters: wait RAW_FULL, split every fp32 word of the
-//                landed tiles in place, x -> hi = tf32_rna(x) (kept where x
-//                was) and lo = tf32_rna(x - hi) (same offset in the stage's lo
-//                tile, so the swizzle carries over), fence.proxy.async, arrive
-//                CONV_FULL.  Linear 16-byte accesses: no bank conflicts.
+//                byte count on RAW_FULL and issues the TMA loads; the first
+//                round of stages is issued before the block-wide barrier.
+//   warp 1       allocates all 512 TMEM columns: chunk accumulators P0, P1,
+//                the running sum S (only when a tile spans several chunks)
+//                and one A slot per stage.  Lane 0 waits CONV_FULL and issues,
+//                per 8-wide k step, P += Alo*Bhi + Ahi*Blo + Ahi*Bhi
+//                (tcgen05.mma kind::tf32, A from TMEM, B from shared memory),
+//                commits EMPTY per stage and CHUNK_FULL per chunk (at most
+//                kChunkKB k-blocks).
+//   warps 2-9    converters (two per TMEM lane quarter, 16 k each): wait
+//                RAW_FULL, split their row of A into the TMEM slot
+//                (tcgen05.st), split B in place (integer round-to-nearest),
+//                fence both proxies, arrive CONV_FULL.
 //   warps 10-13  epilogue: per chunk fold P into S with round-to-nearest fp32
-//                adds (as the register-fed engine does); after the tile's last
-//                chunk, add the bias, write 32 x 32 blocks into 128-byte-
-//                swizzled shared buffers (double-buffered per warp) and store
-//                them with TMA (clipped to the output), so every row leaves
-//                as whole 128-byte lines.
+//                adds; after the tile's last chunk, add the bias, write the
+//                warp's 32 x BN block as 128-byte-swizzled 32 x 32 pieces into
+//                its shared buffer and store them with TMA (clipped to D), so
+//                every row leaves as whole 128-byte lines; the buffer is
+//                rewritten only after those stores have read it.
+//
+// Why chunks: the tensor core's fp32 accumulation rounds on every update, so
+// long reductions fold every 256 k into S (round-to-nearest fp32 adds), as the
+// register-fed engine does.
 //
 // Every mbarrier wait is bounded; on expiry the CTA raises its abort flag,
 // lets TMA loads already issued land, waits for its own TMA stores, frees its
@@ -56,8 +67,10 @@ constexpr int kConvWarps = 8;
 constexpr int kTmaEpiWarp0 = kConvWarp0 + kConvWarps;  // 10 .. 13: lane quarters 2, 3, 0, 1
 constexpr int kTmaThreads = 32 * (kTmaEpiWarp0 + 4);
 constexpr int kTmaMaxStages = 8;
-constexpr int kTmaMaxBN = 128;
+constexpr int kTmaMaxBN = 96;
 constexpr uint32_t kEpiBuf = 32 * 128;  // one 32 x 32 fp32 output block
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kASlotCols = 2 * BK;  // A hi and lo of one k-block
 
 struct TmaProblem {
   int64_t M, N, K;
@@ -66,21 +79,26 @@ struct TmaProblem {
   int bn;
   const float* bias;  // per-column bias, direct mode only
   bool partial;       // out is [splits][M][N] partials (3-D store map)
+  bool use_s;         // some tile spans several chunks: keep a running sum S
 };
+
+// TMEM columns used by the accumulators (P0, P1 and, when needed, S).
+__host__ __device__ inline uint32_t tma_acc_cols(int bn, bool use_s) { return (uint32_t)bn * (use_s ? 3u : 2u); }
 
 struct TmaSmem {
   int stages;
   uint32_t a_bytes, b_bytes, stage_bytes, epi_offset, bar_offset, total;
 };
 
+// Stage = raw A tile + B hi tile + B lo tile.
 __host__ __device__ inline TmaSmem tma_smem_plan(int bn, int stages) {
   TmaSmem s;
   s.stages = stages;
   s.a_bytes = (uint32_t)BM * BK * 4;
   s.b_bytes = (uint32_t)bn * BK * 4;
-  s.stage_bytes = 2 * s.a_bytes + 2 * s.b_bytes;
+  s.stage_bytes = s.a_bytes + 2 * s.b_bytes;
   s.epi_offset = s.stage_bytes * (uint32_t)stages;
-  s.bar_offset = s.epi_offset + 4 * 2 * kEpiBuf;
+  s.bar_offset = s.epi_offset + 4 * (uint32_t)(bn / 32) * kEpiBuf;  // a 32 x BN block per epilogue warp
   s.total = s.bar_offset + 8 * (3 * kTmaMaxStages + 4) + 16 + 1024;  // + alignment slack
   return s;
 }
@@ -126,8 +144,46 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int 
 }
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes; pair with tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Round an fp32 bit pattern to tf32 (10 explicit mantissa bits), to nearest
+// with ties away from zero: add half a tf32 ulp to the magnitude and clear the
+// 13 dropped bits.  Inf and NaN pass through unchanged.
+__device__ __forceinline__ uint32_t tf32_round_bits(uint32_t u) {
+  return (u & 0x7F800000u) == 0x7F800000u ? u : ((u + 0x1000u) & 0xFFFFE000u);
+}
+
+// x -> (hi, lo): hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32).
+__device__ __forceinline__ void split_word(uint4 w, uint4& h, uint4& l) {
+  h.x = tf32_round_bits(w.x);
+  h.y = tf32_round_bits(w.y);
+  h.z = tf32_round_bits(w.z);
+  h.w = tf32_round_bits(w.w);
+  l.x = tf32_round_bits(__float_as_uint(__uint_as_float(w.x) - __uint_as_float(h.x)));
+  l.y = tf32_round_bits(__float_as_uint(__uint_as_float(w.y) - __uint_as_float(h.y)));
+  l.z = tf32_round_bits(__float_as_uint(__uint_as_float(w.z) - __uint_as_float(h.z)));
+  l.w = tf32_round_bits(__float_as_uint(__uint_as_float(w.w) - __uint_as_float(h.w)));
+}
 
 // UMMA shared-memory descriptor with a swizzled layout: type 2 = 128-byte
 // swizzle of 16-byte atoms, type 1 = 128-byte swizzle of 32-byte atoms.
@@ -142,25 +198,47 @@ __host__ __device__ constexpr uint32_t idesc_tf32_major(int n, bool a_mn, bool b
   return idesc_tf32(n) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16);
 }
 
+// D (+)= A * B with A read from tensor memory at column address a_tmem.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 template <bool kAK>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int j) {
   if constexpr (kAK) return smem_desc_swz(base + (uint32_t)j * 32u, 16u, 1024u, 2u);
   else return smem_desc_swz(base + (uint32_t)j * 1024u, 4096u, 512u, 1u);
 }
 
-// Split the 16-byte words [i0, n) step `step` of a landed tile in place.
+// Split the landed words i0, i0 + step, ... (at most N of them, below n) of a
+// tile in place; all loads are issued before the first store.
+template <int N>
 __device__ __forceinline__ void split_words(uint8_t* hi, uint8_t* lo, int n, int i0, int step) {
-  for (int i = i0; i < n; i += step) {
-    const uint4 w = *reinterpret_cast<const uint4*>(hi + 16 * i);
-    const uint32_t h0 = tf32_rna(__uint_as_float(w.x)), h1 = tf32_rna(__uint_as_float(w.y));
-    const uint32_t h2 = tf32_rna(__uint_as_float(w.z)), h3 = tf32_rna(__uint_as_float(w.w));
-    const uint4 l = make_uint4(tf32_rna(__uint_as_float(w.x) - __uint_as_float(h0)),
-                               tf32_rna(__uint_as_float(w.y) - __uint_as_float(h1)),
-                               tf32_rna(__uint_as_float(w.z) - __uint_as_float(h2)),
-                               tf32_rna(__uint_as_float(w.w) - __uint_as_float(h3)));
-    *reinterpret_cast<uint4*>(hi + 16 * i) = make_uint4(h0, h1, h2, h3);
-    *reinterpret_cast<uint4*>(lo + 16 * i) = l;
-  }
+  uint4 w[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (i0 + j * step < n) w[j] = *reinterpret_cast<const uint4*>(hi + 16 * (i0 + j * step));
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (i0 + j * step < n) {
+      uint4 h, l;
+      split_word(w[j], h, l);
+      *reinterpret_cast<uint4*>(hi + 16 * (i0 + j * step)) = h;
+      *reinterpret_cast<uint4*>(lo + 16 * (i0 + j * step)) = l;
+    }
 }
 
 struct TmaTile {
@@ -181,6 +259,48 @@ __device__ __forceinline__ TmaTile tma_tile(const TmaProblem& p, int64_t t) {
   if (c.k_end > p.K) c.k_end = p.K;
   c.nkb = c.k_end > c.k_begin ? (int)((c.k_end - c.k_begin + BK - 1) / BK) : 0;
   return c;
+}
+
+// Loads of one k-block (raw A tile 128 x 32, B tile BN x 32) into a stage.
+template <bool kAK, bool kBK>
+__device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUtensorMap* map_b, uint32_t st,
+                                            uint32_t a_bytes, uint64_t* bar, uint32_t tx, const TmaTile& tc, int kb,
+                                            int bn) {
+  const uint32_t b_hi = st + a_bytes;
+  const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
+  mbar_expect_tx(bar, tx);
+  if constexpr (kAK) {
+    tma_load_2d(st, map_a, k0, (int)tc.m0, bar);
+  } else {
+#pragma unroll
+    for (int b = 0; b < BM / 32; ++b) tma_load_2d(st + 4096u * b, map_a, (int)tc.m0 + 32 * b, k0, bar);
+  }
+  if constexpr (kBK) {
+    tma_load_2d(b_hi, map_b, k0, (int)tc.n0, bar);
+  } else {
+    for (int b = 0; b < bn / 32; ++b) tma_load_2d(b_hi + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
+  }
+}
+
+// Row r, k = 16h .. 16h+15 of a landed raw A tile.
+template <bool kAK>
+__device__ __forceinline__ void read_a_row(const uint8_t* raw, int r, int h, float (&v)[16]) {
+  if constexpr (kAK) {
+    // [128 rows][128 B], 16-byte chunk j of row r at chunk position j ^ (r & 7)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 q = *reinterpret_cast<const float4*>(raw + r * 128 + (((4 * h + j) ^ (r & 7)) << 4));
+      v[4 * j] = q.x;
+      v[4 * j + 1] = q.y;
+      v[4 * j + 2] = q.z;
+      v[4 * j + 3] = q.w;
+    }
+  } else {
+    // [4 blocks][32 k][32 rows]
+    const float* col = reinterpret_cast<const float*>(raw + (r >> 5) * 4096) + (r & 31);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = col[(16 * h + i) * 32];
+  }
 }
 
 template <bool kAK, bool kBK>
@@ -205,10 +325,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int64_t nt = (p.N + bn - 1) / bn, mt = (p.M + BM - 1) / BM;
   const int64_t tiles = nt * mt * p.splits;
   const uint32_t acc_cols = (uint32_t)bn;
-  const int need_cols = 3 * bn;  // P0, P1, S
-  const uint32_t tmem_cols = need_cols <= 32 ? 32u : need_cols <= 64 ? 64u : need_cols <= 128 ? 128u
-                             : need_cols <= 256 ? 256u : 512u;
+  const uint32_t a_col0 = tma_acc_cols(bn, p.use_s);  // first A slot column
+  const uint32_t tx = plan.a_bytes + plan.b_bytes;
 
+  // TMA issue cursor (lane 0 of warp 0): tile t, k-block kb, stage use it.
+  int64_t t_iss = blockIdx.x;
+  int kb_iss = 0;
+  uint32_t it_iss = 0;
+  TmaTile tc_iss{};
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < stages; ++s) {
@@ -221,10 +345,26 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       mbar_init(&chunk_empty[a], 128);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&map_a);
+    prefetch_map(&map_b);
+    prefetch_map(&map_d);
+    // The first round of stages needs no EMPTY wait: issue it before the
+    // block-wide barrier so the loads overlap the TMEM allocation.
+    if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
+    while (t_iss < tiles && it_iss < (uint32_t)stages) {
+      issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)it_iss * plan.stage_bytes), plan.a_bytes,
+                            &raw_full[it_iss], tx, tc_iss, kb_iss, bn);
+      ++it_iss;
+      if (++kb_iss == tc_iss.nkb) {
+        kb_iss = 0;
+        t_iss += gridDim.x;
+        if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
+      }
+    }
   }
   if (warp == kTmaMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(tmem_cols)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -236,44 +376,33 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   if (warp == kTmaWarp) {
     // ---------------------------------------------------------- TMA issue
     if (lane == 0) {
-      const uint32_t tx = plan.a_bytes + plan.b_bytes;
-      uint32_t it = 0;
-      bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const TmaTile tc = tma_tile(p, t);
-        for (int kb = 0; kb < tc.nkb; ++kb, ++it) {
-          const int s = (int)(it % (uint32_t)stages);
-          const uint32_t round = it / (uint32_t)stages;
-          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t st = smem_u32(smem + (size_t)s * plan.stage_bytes);
-          const uint32_t a_hi = st, b_hi = st + 2u * plan.a_bytes;
-          const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
-          mbar_expect_tx(&raw_full[s], tx);
-          if constexpr (kAK) {
-            tma_load_2d(a_hi, &map_a, k0, (int)tc.m0, &raw_full[s]);
-          } else {
-#pragma unroll
-            for (int b = 0; b < BM / 32; ++b) tma_load_2d(a_hi + 4096u * b, &map_a, (int)tc.m0 + 32 * b, k0, &raw_full[s]);
-          }
-          if constexpr (kBK) {
-            tma_load_2d(b_hi, &map_b, k0, (int)tc.n0, &raw_full[s]);
-          } else {
-            for (int b = 0; b < bn / 32; ++b) tma_load_2d(b_hi + 4096u * b, &map_b, (int)tc.n0 + 32 * b, k0, &raw_full[s]);
-          }
+      while (t_iss < tiles) {
+        const int s = (int)(it_iss % (uint32_t)stages);
+        const uint32_t round = it_iss / (uint32_t)stages;
+        if (!mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) break;
+        issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.stage_bytes), plan.a_bytes,
+                              &raw_full[s], tx, tc_iss, kb_iss, bn);
+        ++it_iss;
+        if (++kb_iss == tc_iss.nkb) {
+          kb_iss = 0;
+          t_iss += gridDim.x;
+          if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
         }
       }
       // Let every issued load land before the CTA can exit.
-      const uint32_t n = it < (uint32_t)stages ? it : (uint32_t)stages;
-      for (uint32_t i = it - n; i < it; ++i) mbar_wait_drain(&raw_full[i % (uint32_t)stages], (i / (uint32_t)stages) & 1u);
+      const uint32_t n = it_iss < (uint32_t)stages ? it_iss : (uint32_t)stages;
+      for (uint32_t i = it_iss - n; i < it_iss; ++i)
+        mbar_wait_drain(&raw_full[i % (uint32_t)stages], (i / (uint32_t)stages) & 1u);
     }
   } else if (warp >= kConvWarp0 && warp < kTmaEpiWarp0) {
     // ---------------------------------------------------------- converters
     const int ct = threadIdx.x - 32 * kConvWarp0;
     constexpr int nct = kConvWarps * 32;
-    const int a_words = (int)(plan.a_bytes / 16), b_words = (int)(plan.b_bytes / 16);
+    const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31 = A rows
+    const int half = (warp - kConvWarp0) >> 2;  // k 16*half .. +15
+    const int row = quarter * 32 + lane;
+    const uint32_t a_taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + a_col0 + (uint32_t)(16 * half);
+    const int b_words = bn * BK * 4 / 16;
     uint32_t it = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -285,17 +414,29 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           break;
         }
         uint8_t* st = smem + (size_t)s * plan.stage_bytes;
-        split_words(st, st + plan.a_bytes, a_words, ct, nct);
-        uint8_t* bh = st + 2 * plan.a_bytes;
-        split_words(bh, bh + plan.b_bytes, b_words, ct, nct);
+        float v[16];
+        read_a_row<kAK>(st, row, half, v);
+        uint32_t hv[16], lv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          hv[i] = tf32_round_bits(__float_as_uint(v[i]));
+          lv[i] = tf32_round_bits(__float_as_uint(v[i] - __uint_as_float(hv[i])));
+        }
+        const uint32_t slot = a_taddr + (uint32_t)s * kASlotCols;
+        tmem_st16u(slot, hv);
+        tmem_st16u(slot + BK, lv);
+        uint8_t* bh = st + plan.a_bytes;
+        split_words<kTmaMaxBN * BK * 4 / 16 / nct>(bh, bh + plan.b_bytes, b_words, ct, nct);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(&conv_full[s]);
       }
     }
   } else if (warp == kTmaMmaWarp) {
     // -------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32_major(bn, !kAK, !kBK);
+      const uint32_t idesc = idesc_tf32_major(bn, false, !kBK);
       uint32_t it = 0, g = 0;  // g counts chunks
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
@@ -317,15 +458,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t st = smem_u32(smem + (size_t)s * plan.stage_bytes);
-            const uint32_t a_hi = st, a_lo = st + plan.a_bytes;
-            const uint32_t b_hi = st + 2u * plan.a_bytes, b_lo = b_hi + plan.b_bytes;
+            const uint32_t a_hi = tmem_base + a_col0 + (uint32_t)s * kASlotCols, a_lo = a_hi + BK;
+            const uint32_t b_hi = smem_u32(smem + (size_t)s * plan.stage_bytes) + plan.a_bytes;
+            const uint32_t b_lo = b_hi + plan.b_bytes;
 #pragma unroll
             for (int j = 0; j < BK / 8; ++j) {
-              mma_tf32(d, operand_desc<kAK>(a_lo, j), operand_desc<kBK>(b_hi, j), idesc,
-                       (kb > kb0 || j > 0) ? 1u : 0u);
-              mma_tf32(d, operand_desc<kAK>(a_hi, j), operand_desc<kBK>(b_lo, j), idesc, 1u);
-              mma_tf32(d, operand_desc<kAK>(a_hi, j), operand_desc<kBK>(b_hi, j), idesc, 1u);
+              mma_tf32_ts(d, a_lo + 8u * j, operand_desc<kBK>(b_hi, j), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+              mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_lo, j), idesc, 1u);
+              mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_hi, j), idesc, 1u);
             }
             mma_commit(&empty[s]);
           }
@@ -338,9 +478,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_off + 2u * acc_cols;
-    uint8_t* ebuf = smem + plan.epi_offset + (size_t)(warp - kTmaEpiWarp0) * 2 * kEpiBuf;
-    uint32_t g = 0, nstore = 0;
-    bool ok = true;
+    uint8_t* ebuf = smem + plan.epi_offset + (size_t)(warp - kTmaEpiWarp0) * (bn / 32) * kEpiBuf;
+    uint32_t g = 0;
+    bool ok = true, pending = false;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       const TmaTile tc = tma_tile(p, t);
       const int nch = (tc.nkb + kChunkKB - 1) / kChunkKB;
@@ -355,62 +495,67 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         }
+        if (last && pending) {  // the previous tile's stores must have read the buffer
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          pending = false;
+        }
         const uint32_t p_addr = tmem_base + lane_off + (uint32_t)a * acc_cols;
         for (int c = 0; c < bn; c += 32) {
           float v[32];
+          if (nch > 0) {
+            uint32_t pv[32];
+            tmem_ld32(p_addr + (uint32_t)c, pv);
+            if (!first) {
+              uint32_t sv[32];
+              tmem_ld32(s_addr + (uint32_t)c, sv);
+              tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float* vh = v + 16 * h;
-            if (nch > 0) {
-              float pv[16];
-              tmem_ld16(p_addr + (uint32_t)(c + 16 * h), pv);
-              if (!first) {
-                float sv[16];
-                tmem_ld16(s_addr + (uint32_t)(c + 16 * h), sv);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) pv[e] = __fadd_rn(sv[e], pv[e]);
-              }
-              if (!last) tmem_st16(s_addr + (uint32_t)(c + 16 * h), pv);
-#pragma unroll
-              for (int e = 0; e < 16; ++e) vh[e] = pv[e];
+              for (int e = 0; e < 32; ++e) v[e] = __fadd_rn(__uint_as_float(sv[e]), __uint_as_float(pv[e]));
             } else {
+              tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) vh[e] = 0.0f;
+              for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(pv[e]);
             }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = 0.0f;
           }
-          if (!last) continue;
+          if (!last) {
+            tmem_st16(s_addr + (uint32_t)c, *reinterpret_cast<const float(*)[16]>(v));
+            tmem_st16(s_addr + (uint32_t)c + 16u, *reinterpret_cast<const float(*)[16]>(v + 16));
+            continue;
+          }
           if (p.bias) {
             const int64_t n = tc.n0 + c;
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (n + e < p.N) v[e] += __ldg(p.bias + n + e);
           }
-          if (row0 >= p.M || tc.n0 + c >= p.N) continue;  // block wholly outside D
-          // 32 x 32 block -> swizzled buffer -> TMA store
-          const uint32_t b = nstore & 1u;
-          if (nstore >= 2) {
-            if (lane == 0) bulk_wait_read1();
-            __syncwarp();
-          }
-          uint8_t* buf = ebuf + b * kEpiBuf;
+          uint8_t* buf = ebuf + (c / 32) * kEpiBuf;  // 32 x 32 block, 128-byte swizzled rows
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) {
-            if (p.partial) tma_store_3d(&map_d, (int)tc.n0 + c, row0, tc.z, smem_u32(buf));
-            else tma_store_2d(&map_d, (int)tc.n0 + c, row0, smem_u32(buf));
-            bulk_commit();
-          }
-          ++nstore;
         }
         if (nch > 0) {
           if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           mbar_arrive(&chunk_empty[a]);  // P may be refilled
           ++g;
+        }
+        if (last) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && row0 < p.M) {
+            for (int c = 0; c < bn && tc.n0 + c < p.N; c += 32) {
+              const uint32_t src = smem_u32(ebuf + (c / 32) * kEpiBuf);
+              if (p.partial) tma_store_3d(&map_d, (int)tc.n0 + c, row0, tc.z, src);
+              else tma_store_2d(&map_d, (int)tc.n0 + c, row0, src);
+            }
+            bulk_commit();
+          }
+          pending = true;
         }
       }
     }
@@ -421,7 +566,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   if (warp == kTmaMmaWarp) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
                  : "memory");
   }
 }
