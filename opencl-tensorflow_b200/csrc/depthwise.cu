@@ -10,11 +10,13 @@
 //     (kh, kw[, d]) order with round-to-nearest multiply and add, so every
 //     output is bit-identical to the reference's sequential fp32 sum;
 //   other shapes: one thread per element, same order, same exactness;
+//   input gradient, dm == 1 and C % 4 == 0: one CTA per input row (decoded
+//     once), threads over (pixel of the row, 4 channels), same order;
 //   filter gradient: a sum over N*Ho*Wo per filter element, done as per-CTA
 //     partial sums (each thread owns 4 channels x all taps, CTAs fold their
-//     pixel lanes in a fixed order) plus a fixed-order finalize, so it is
-//     deterministic; with dm > 1 or C % 4 != 0 a scalar variant of the same
-//     two stages.
+//     pixel lanes in a fixed order) plus a finalize that adds the partials in
+//     a fixed tree, so it is deterministic; with dm > 1 or C % 4 != 0 a
+//     scalar variant of the same two stages.
 #include "conv_common.cuh"
 
 namespace b2 {
@@ -28,6 +30,11 @@ __device__ __forceinline__ float4 fadd4(float4 a, float4 b) {
 __device__ __forceinline__ float4 fmul4(float4 a, float4 b) {
   return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
 }
+
+// x / s for x >= 0 and a small runtime stride s (1 and 2, the common cases,
+// need no division); x % s likewise.
+__device__ __forceinline__ int div_stride(int x, int s) { return s == 1 ? x : s == 2 ? (x >> 1) : x / s; }
+__device__ __forceinline__ int mod_stride(int x, int s) { return s == 1 ? 0 : s == 2 ? (x & 1) : x % s; }
 
 struct DwArgs {
   int N, H, W, C, kH, kW, dm, sH, sW, pH, pW, Ho, Wo;
@@ -110,42 +117,42 @@ __global__ void __launch_bounds__(kThreads) dw_fwd_scalar_kernel(const float* __
 
 // ----------------------------------------------------------- input grad
 
-// depthwise_conv2d_kernels.cl:59-104, dm == 1, 4 channels per thread.
-__global__ void __launch_bounds__(kThreads) dw_dgrad_vec4_kernel(const float* __restrict__ dy,
+// depthwise_conv2d_kernels.cl:59-104, dm == 1, 4 channels per thread: CTA =
+// input row (n, hi); thread (x, y) = (channel group, input column lane).
+__global__ void __launch_bounds__(kThreads) dw_dgrad_rows_kernel(const float* __restrict__ dy,
                                                                   const float* __restrict__ w,
                                                                   float* __restrict__ dx, DwArgs a) {
   const int cg = a.C >> 2;
-  const int64_t total = (int64_t)a.N * a.H * a.W * cg;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < total; g += stride) {
-    uint32_t p = (uint32_t)g / (uint32_t)cg;  // element counts < 2^31 (checked on the host)
-    const int c = (int)((uint32_t)g - p * (uint32_t)cg) * 4;
-    uint32_t q = p / (uint32_t)a.W;
-    const int wi = (int)(p - q * (uint32_t)a.W);
-    const uint32_t n32 = q / (uint32_t)a.H;
-    const int hi = (int)(q - n32 * (uint32_t)a.H);
-    const int n = (int)n32;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    // Only taps with (hi + pH - kh) % sH == 0 reach this pixel: start at the
-    // first such kh and step by the stride (ascending, as the reference).
-    const int kh0 = (hi + a.pH) % a.sH, kw0 = (wi + a.pW) % a.sW;
-    for (int kh = kh0; kh < a.kH; kh += a.sH) {
-      const int hn = hi + a.pH - kh;
-      if (hn < 0) break;
-      const int ho = hn / a.sH;
-      if (ho >= a.Ho) continue;
-      for (int kw = kw0; kw < a.kW; kw += a.sW) {
-        const int wn = wi + a.pW - kw;
-        if (wn < 0) break;
-        const int wo = wn / a.sW;
-        if (wo >= a.Wo) continue;
-        const float4 gv =
-            __ldg(reinterpret_cast<const float4*>(dy + ((int64_t)(n * a.Ho + ho) * a.Wo + wo) * a.C + c));
-        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)(kh * a.kW + kw) * a.C + c));
-        acc = fadd4(acc, fmul4(gv, wv));
+  const int row = blockIdx.x;  // n * H + hi (< 2^31, checked on the host)
+  const int n = row / a.H, hi = row - n * a.H;
+  const float* gimg = dy + (int64_t)n * a.Ho * a.Wo * a.C;
+  // Only taps with (hi + pH - kh) % sH == 0 reach this row: start at the
+  // first such kh and step by the stride (ascending, as the reference).
+  const int kh0 = mod_stride(hi + a.pH, a.sH);
+  for (int wi = threadIdx.y; wi < a.W; wi += blockDim.y) {
+    const int kw0 = mod_stride(wi + a.pW, a.sW);
+    float* xp = dx + ((int64_t)row * a.W + wi) * a.C;
+    for (int c4 = threadIdx.x; c4 < cg; c4 += blockDim.x) {
+      const int c = 4 * c4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int kh = kh0; kh < a.kH; kh += a.sH) {
+        const int hn = hi + a.pH - kh;
+        if (hn < 0) break;
+        const int ho = div_stride(hn, a.sH);
+        if (ho >= a.Ho) continue;
+        const float* grow = gimg + (int64_t)ho * a.Wo * a.C + c;
+        for (int kw = kw0; kw < a.kW; kw += a.sW) {
+          const int wn = wi + a.pW - kw;
+          if (wn < 0) break;
+          const int wo = div_stride(wn, a.sW);
+          if (wo >= a.Wo) continue;
+          const float4 gv = __ldg(reinterpret_cast<const float4*>(grow + (int64_t)wo * a.C));
+          const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)(kh * a.kW + kw) * a.C + c));
+          acc = fadd4(acc, fmul4(gv, wv));
+        }
       }
+      *reinterpret_cast<float4*>(xp + c) = acc;
     }
-    reinterpret_cast<float4*>(dx)[g] = acc;
   }
 }
 
@@ -296,14 +303,36 @@ __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_scalar_kernel(const
   partial[(int64_t)blockIdx.x * F + f] = acc;
 }
 
-// Stage 2: dw[f] = sum over blocks of partial[b][f], in block order.
-__global__ void dw_wgrad_finalize_kernel(const float* __restrict__ partial, int blocks, int F,
-                                         float* __restrict__ dw) {
-  const int f = blockIdx.x * blockDim.x + threadIdx.x;
-  if (f >= F) return;
-  float s = 0.0f;
-  for (int b = 0; b < blocks; ++b) s += partial[(int64_t)b * F + f];
-  dw[f] = s;
+// Stage 2: dw[f] = sum over blocks of partial[b][f] in a fixed order: CTA of
+// 32 x 32 threads per 32 filter elements; part j adds blocks j, j+32, ... in
+// order, then the 32 part sums are added in part order.
+constexpr int kFinParts = 32;
+__global__ void __launch_bounds__(32 * kFinParts) dw_wgrad_finalize_kernel(const float* __restrict__ partial,
+                                                                           int blocks, int F,
+                                                                           float* __restrict__ dw) {
+  __shared__ float s_part[kFinParts][32];
+  const int f = blockIdx.x * 32 + threadIdx.x;
+  const int part = threadIdx.y;
+  float acc = 0.0f;
+  if (f < F) {
+#pragma unroll 4
+    for (int b = part; b < blocks; b += kFinParts) acc += __ldg(partial + (int64_t)b * F + f);
+  }
+  s_part[part][threadIdx.x] = acc;
+  __syncthreads();
+  if (part == 0 && f < F) {
+    float sum = s_part[0][threadIdx.x];
+    for (int j = 1; j < kFinParts; ++j) sum += s_part[j][threadIdx.x];
+    dw[f] = sum;
+  }
+}
+
+// Threads of a row CTA: x over channel groups, y over pixels of the row.
+dim3 row_block(int cg, int64_t width) {
+  const int bx = cg < kThreads ? cg : kThreads;
+  int by = kThreads / bx;
+  if (by > width) by = (int)(width > 0 ? width : 1);
+  return dim3((unsigned)bx, (unsigned)by);
 }
 
 int dw_forward_geom(const int64_t* input_shape, const int64_t* filter_shape, const int32_t* strides,
@@ -385,8 +414,8 @@ int b2_depthwise_conv2d_backprop_input(b2_stream_t stream, const int32_t input_s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const DwArgs a = to_args(g);
   if (g.dm == 1 && g.Ci % 4 == 0 && aligned16(out_backprop) && aligned16(filter) && aligned16(output)) {
-    dw_dgrad_vec4_kernel<<<grid_for(g.in_elems() / 4, kThreads, 8), kThreads, 0, s>>>(out_backprop, filter,
-                                                                                      output, a);
+    dw_dgrad_rows_kernel<<<(unsigned)(g.N * g.H), row_block((int)(g.Ci / 4), g.W), 0, s>>>(out_backprop, filter,
+                                                                                          output, a);
   } else {
     dw_dgrad_scalar_kernel<<<grid_for(g.in_elems(), kThreads, 8), kThreads, 0, s>>>(out_backprop, filter,
                                                                                     output, a);
@@ -450,7 +479,8 @@ int b2_depthwise_conv2d_backprop_filter(b2_stream_t stream, const float* input, 
         input, out_backprop, part.as<float>(), a, ppb);
   }
   B2_RETURN_IF_ERROR(check_launch(s, "dwconv2d_backprop_filter"));
-  dw_wgrad_finalize_kernel<<<(int)ceil_div(F, 256), 256, 0, s>>>(part.as<float>(), blocks, (int)F, output);
+  dw_wgrad_finalize_kernel<<<(unsigned)ceil_div(F, 32), dim3(32, kFinParts), 0, s>>>(part.as<float>(), blocks,
+                                                                                       (int)F, output);
   return check_launch(s, "dwconv2d_backprop_filter_finalize");
 }
 

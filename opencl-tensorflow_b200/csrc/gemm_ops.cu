@@ -389,27 +389,29 @@ int tma_bn(int64_t N) {
   return (int)(ceil_div(ceil_div(N, tiles), 32) * 32);
 }
 
-// Stages: limited by shared memory and by the TMEM columns left for A slots.
-int tma_stages(int bn, bool use_s, int max_smem) {
-  const TmaSmem fixed = tma_smem_plan(bn, 0);
-  int st = (int)((max_smem - (int)fixed.total) / (int)fixed.stage_bytes);
-  const int by_tmem = (int)((kTmemCols - tma_acc_cols(bn, use_s)) / kASlotCols);
-  if (st > by_tmem) st = by_tmem;
-  if (st > kTmaMaxStages) st = kTmaMaxStages;
-  return st;
+// Operand stages: limited by the TMEM columns left for A slots; raw stages
+// take the remaining shared memory.
+void tma_stages(int bn, bool use_s, int max_smem, int* raw_stages, int* op_stages) {
+  int q = (int)((kTmemCols - tma_acc_cols(bn, use_s)) / kASlotCols);
+  if (q > kTmaMaxOpStages) q = kTmaMaxOpStages;
+  const TmaSmem fixed = tma_smem_plan(bn, 0, q);
+  int r = (int)((max_smem - (int)fixed.total) / (int)fixed.raw_bytes);
+  if (r > kTmaMaxStages) r = kTmaMaxStages;
+  *raw_stages = r;
+  *op_stages = q;
 }
 
 template <bool kAK, bool kBK>
 int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
-               int stages, int grid, cudaStream_t s, const char* name) {
-  const TmaSmem plan = tma_smem_plan(prob.bn, stages);
+               int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
+  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages);
   static int configured_bytes = 0;  // per instantiation
   if ((int)plan.total > configured_bytes) {
     B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<kAK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)plan.total));
     configured_bytes = (int)plan.total;
   }
-  tma_gemm_kernel<kAK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, stages);
+  tma_gemm_kernel<kAK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, raw_stages, op_stages);
   return check_launch(s, name);
 }
 
@@ -424,8 +426,10 @@ int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N,
   if (kps < BK) kps = BK;
   splits = (int)ceil_div(K, kps);
   const bool use_s = kps > (int64_t)kChunkKB * BK;
-  const int stages = tma_stages(bn, use_s, d->max_smem_optin);
-  if (stages < 2) return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
+  int raw_stages = 0, op_stages = 0;
+  tma_stages(bn, use_s, d->max_smem_optin, &raw_stages, &op_stages);
+  if (raw_stages < 2 || op_stages < 2)
+    return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
   TmaProblem prob{M, N, K, kps, splits, bn, bias, false, use_s};
   CUtensorMap ma, mb, md;
   B2_RETURN_IF_ERROR(encode_operand(&ma, a, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
@@ -446,10 +450,10 @@ int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N,
   }
   const int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
   int rc;
-  if (a.k_major && b.k_major) rc = launch_tma<true, true>(ma, mb, md, prob, stages, grid, s, name);
-  else if (a.k_major) rc = launch_tma<true, false>(ma, mb, md, prob, stages, grid, s, name);
-  else if (b.k_major) rc = launch_tma<false, true>(ma, mb, md, prob, stages, grid, s, name);
-  else rc = launch_tma<false, false>(ma, mb, md, prob, stages, grid, s, name);
+  if (a.k_major && b.k_major) rc = launch_tma<true, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+  else if (a.k_major) rc = launch_tma<true, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+  else if (b.k_major) rc = launch_tma<false, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+  else rc = launch_tma<false, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
   B2_RETURN_IF_ERROR(rc);
   if (splits == 1) return B2_OK;
   splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);

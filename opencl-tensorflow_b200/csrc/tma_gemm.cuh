@@ -66,7 +66,8 @@ constexpr int kConvWarp0 = 2;
 constexpr int kConvWarps = 8;
 constexpr int kTmaEpiWarp0 = kConvWarp0 + kConvWarps;  // 10 .. 13: lane quarters 2, 3, 0, 1
 constexpr int kTmaThreads = 32 * (kTmaEpiWarp0 + 4);
-constexpr int kTmaMaxStages = 8;
+constexpr int kTmaMaxStages = 8;    // raw (TMA) stages
+constexpr int kTmaMaxOpStages = 4;  // operand stages (B hi/lo in smem + A hi/lo in TMEM)
 constexpr int kTmaMaxBN = 96;
 constexpr uint32_t kEpiBuf = 32 * 128;  // one 32 x 32 fp32 output block
 constexpr uint32_t kTmemCols = 512;
@@ -86,20 +87,25 @@ struct TmaProblem {
 __host__ __device__ inline uint32_t tma_acc_cols(int bn, bool use_s) { return (uint32_t)bn * (use_s ? 3u : 2u); }
 
 struct TmaSmem {
-  int stages;
-  uint32_t a_bytes, b_bytes, stage_bytes, epi_offset, bar_offset, total;
+  int raw_stages, op_stages;
+  uint32_t a_bytes, b_bytes, raw_bytes, op_bytes, op_offset, epi_offset, bar_offset, total;
 };
 
-// Stage = raw A tile + B hi tile + B lo tile.
-__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int stages) {
+// Shared memory: a ring of raw stages (TMA destinations: raw A tile + raw B
+// tile), a ring of operand stages (B hi tile + B lo tile, read by the MMA),
+// the epilogue buffers and the barriers.
+__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_stages) {
   TmaSmem s;
-  s.stages = stages;
+  s.raw_stages = raw_stages;
+  s.op_stages = op_stages;
   s.a_bytes = (uint32_t)BM * BK * 4;
   s.b_bytes = (uint32_t)bn * BK * 4;
-  s.stage_bytes = s.a_bytes + 2 * s.b_bytes;
-  s.epi_offset = s.stage_bytes * (uint32_t)stages;
+  s.raw_bytes = s.a_bytes + s.b_bytes;
+  s.op_bytes = 2 * s.b_bytes;
+  s.op_offset = s.raw_bytes * (uint32_t)raw_stages;
+  s.epi_offset = s.op_offset + s.op_bytes * (uint32_t)op_stages;
   s.bar_offset = s.epi_offset + 4 * (uint32_t)(bn / 32) * kEpiBuf;  // a 32 x BN block per epilogue warp
-  s.total = s.bar_offset + 8 * (3 * kTmaMaxStages + 4) + 16 + 1024;  // + alignment slack
+  s.total = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4) + 16 + 1024;  // + alignment slack
   return s;
 }
 
@@ -261,12 +267,13 @@ __device__ __forceinline__ TmaTile tma_tile(const TmaProblem& p, int64_t t) {
   return c;
 }
 
-// Loads of one k-block (raw A tile 128 x 32, B tile BN x 32) into a stage.
+// Loads of one k-block (raw A tile 128 x 32, raw B tile BN x 32) into a raw
+// stage.
 template <bool kAK, bool kBK>
 __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUtensorMap* map_b, uint32_t st,
                                             uint32_t a_bytes, uint64_t* bar, uint32_t tx, const TmaTile& tc, int kb,
                                             int bn) {
-  const uint32_t b_hi = st + a_bytes;
+  const uint32_t b_raw = st + a_bytes;
   const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
   mbar_expect_tx(bar, tx);
   if constexpr (kAK) {
@@ -276,9 +283,9 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
     for (int b = 0; b < BM / 32; ++b) tma_load_2d(st + 4096u * b, map_a, (int)tc.m0 + 32 * b, k0, bar);
   }
   if constexpr (kBK) {
-    tma_load_2d(b_hi, map_b, k0, (int)tc.n0, bar);
+    tma_load_2d(b_raw, map_b, k0, (int)tc.n0, bar);
   } else {
-    for (int b = 0; b < bn / 32; ++b) tma_load_2d(b_hi + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
+    for (int b = 0; b < bn / 32; ++b) tma_load_2d(b_raw + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
   }
 }
 
@@ -303,19 +310,32 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, int r, int h, flo
   }
 }
 
+__device__ __forceinline__ void split16(const float (&v)[16], uint32_t (&hv)[16], uint32_t (&lv)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    hv[i] = tf32_round_bits(__float_as_uint(v[i]));
+    lv[i] = tf32_round_bits(__float_as_uint(v[i] - __uint_as_float(hv[i])));
+  }
+}
+
+constexpr int kGroupThreads = 128;  // one converter group: a warp per TMEM lane quarter
+constexpr int kMaxBWords = kTmaMaxBN * BK * 4 / 16 / kGroupThreads;  // 16-byte B words per thread
+
 template <bool kAK, bool kBK>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     tma_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    const __grid_constant__ CUtensorMap map_d, const TmaProblem p, const int stages) {
+                    const __grid_constant__ CUtensorMap map_d, const TmaProblem p, const int raw_stages,
+                    const int op_stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
-  const TmaSmem plan = tma_smem_plan(bn, stages);
+  const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages);
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + plan.bar_offset);
-  uint64_t* conv_full = raw_full + kTmaMaxStages;
-  uint64_t* empty = conv_full + kTmaMaxStages;
-  uint64_t* chunk_full = empty + kTmaMaxStages;  // [2]
-  uint64_t* chunk_empty = chunk_full + 2;        // [2]
+  uint64_t* raw_empty = raw_full + kTmaMaxStages;
+  uint64_t* op_full = raw_empty + kTmaMaxStages;
+  uint64_t* op_empty = op_full + kTmaMaxOpStages;
+  uint64_t* chunk_full = op_empty + kTmaMaxOpStages;  // [2]
+  uint64_t* chunk_empty = chunk_full + 2;             // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
@@ -326,19 +346,23 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int64_t tiles = nt * mt * p.splits;
   const uint32_t acc_cols = (uint32_t)bn;
   const uint32_t a_col0 = tma_acc_cols(bn, p.use_s);  // first A slot column
-  const uint32_t tx = plan.a_bytes + plan.b_bytes;
+  const uint32_t tx = plan.raw_bytes;
+  const uint32_t R = (uint32_t)raw_stages, Q = (uint32_t)op_stages;
 
-  // TMA issue cursor (lane 0 of warp 0): tile t, k-block kb, stage use it.
+  // TMA issue cursor (lane 0 of warp 0): tile t, k-block kb, raw stage use it.
   int64_t t_iss = blockIdx.x;
   int kb_iss = 0;
   uint32_t it_iss = 0;
   TmaTile tc_iss{};
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int s = 0; s < stages; ++s) {
+    for (int s = 0; s < raw_stages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&conv_full[s], kConvWarps * 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&raw_empty[s], 4);
+    }
+    for (int s = 0; s < op_stages; ++s) {
+      mbar_init(&op_full[s], 4);
+      mbar_init(&op_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&chunk_full[a], 1);
@@ -348,11 +372,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     prefetch_map(&map_a);
     prefetch_map(&map_b);
     prefetch_map(&map_d);
-    // The first round of stages needs no EMPTY wait: issue it before the
+    // The first round of raw stages needs no EMPTY wait: issue it before the
     // block-wide barrier so the loads overlap the TMEM allocation.
     if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
-    while (t_iss < tiles && it_iss < (uint32_t)stages) {
-      issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)it_iss * plan.stage_bytes), plan.a_bytes,
+    while (t_iss < tiles && it_iss < R) {
+      issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)it_iss * plan.raw_bytes), plan.a_bytes,
                             &raw_full[it_iss], tx, tc_iss, kb_iss, bn);
       ++it_iss;
       if (++kb_iss == tc_iss.nkb) {
@@ -377,10 +401,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     // ---------------------------------------------------------- TMA issue
     if (lane == 0) {
       while (t_iss < tiles) {
-        const int s = (int)(it_iss % (uint32_t)stages);
-        const uint32_t round = it_iss / (uint32_t)stages;
-        if (!mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) break;
-        issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.stage_bytes), plan.a_bytes,
+        const uint32_t s = it_iss % R;
+        if (!mbar_wait(&raw_empty[s], (it_iss / R - 1) & 1u, abort_flag)) break;
+        issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.raw_bytes), plan.a_bytes,
                               &raw_full[s], tx, tc_iss, kb_iss, bn);
         ++it_iss;
         if (++kb_iss == tc_iss.nkb) {
@@ -390,47 +413,69 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         }
       }
       // Let every issued load land before the CTA can exit.
-      const uint32_t n = it_iss < (uint32_t)stages ? it_iss : (uint32_t)stages;
-      for (uint32_t i = it_iss - n; i < it_iss; ++i)
-        mbar_wait_drain(&raw_full[i % (uint32_t)stages], (i / (uint32_t)stages) & 1u);
+      const uint32_t n = it_iss < R ? it_iss : R;
+      for (uint32_t i = it_iss - n; i < it_iss; ++i) mbar_wait_drain(&raw_full[i % R], (i / R) & 1u);
     }
   } else if (warp >= kConvWarp0 && warp < kTmaEpiWarp0) {
     // ---------------------------------------------------------- converters
-    const int ct = threadIdx.x - 32 * kConvWarp0;
-    constexpr int nct = kConvWarps * 32;
-    const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31 = A rows
-    const int half = (warp - kConvWarp0) >> 2;  // k 16*half .. +15
+    // Two groups of four warps take alternate k-blocks; in a group, the warp
+    // of lane quarter q converts rows 32q .. 32q+31 of A (one row a thread)
+    // and a share of B's 16-byte words.
+    const int group = (warp - kConvWarp0) >> 2;
+    const int quarter = warp & 3;
+    const int gt = ((warp - kConvWarp0) & 3) * 32 + lane;
     const int row = quarter * 32 + lane;
-    const uint32_t a_taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + a_col0 + (uint32_t)(16 * half);
+    const uint32_t a_taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + a_col0;
     const int b_words = bn * BK * 4 / 16;
-    uint32_t it = 0;
+    uint32_t i = 0;  // k-block sequence number
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       const TmaTile tc = tma_tile(p, t);
-      for (int kb = 0; kb < tc.nkb; ++kb, ++it) {
-        const int s = (int)(it % (uint32_t)stages);
-        if (!mbar_wait(&raw_full[s], (it / (uint32_t)stages) & 1u, abort_flag)) {
+      for (int kb = 0; kb < tc.nkb; ++kb, ++i) {
+        if ((int)(i & 1u) != group) continue;
+        const uint32_t sr = i % R, sq = i % Q;
+        if (!mbar_wait(&raw_full[sr], (i / R) & 1u, abort_flag)) {
           ok = false;
           break;
         }
-        uint8_t* st = smem + (size_t)s * plan.stage_bytes;
-        float v[16];
-        read_a_row<kAK>(st, row, half, v);
-        uint32_t hv[16], lv[16];
+        const uint8_t* raw = smem + (size_t)sr * plan.raw_bytes;
+        float va[2][16];
+        read_a_row<kAK>(raw, row, 0, va[0]);
+        read_a_row<kAK>(raw, row, 1, va[1]);
+        uint4 wb[kMaxBWords];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          hv[i] = tf32_round_bits(__float_as_uint(v[i]));
-          lv[i] = tf32_round_bits(__float_as_uint(v[i] - __uint_as_float(hv[i])));
+        for (int j = 0; j < kMaxBWords; ++j)
+          if (gt + j * kGroupThreads < b_words)
+            wb[j] = *reinterpret_cast<const uint4*>(raw + plan.a_bytes + 16 * (gt + j * kGroupThreads));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[sr]);  // this warp has read the raw stage
+        if (i >= Q && !mbar_wait(&op_empty[sq], (i / Q - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
         }
-        const uint32_t slot = a_taddr + (uint32_t)s * kASlotCols;
-        tmem_st16u(slot, hv);
-        tmem_st16u(slot + BK, lv);
-        uint8_t* bh = st + plan.a_bytes;
-        split_words<kTmaMaxBN * BK * 4 / 16 / nct>(bh, bh + plan.b_bytes, b_words, ct, nct);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t slot = a_taddr + sq * kASlotCols;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t hv[16], lv[16];
+          split16(va[h], hv, lv);
+          tmem_st16u(slot + 16u * h, hv);
+          tmem_st16u(slot + BK + 16u * h, lv);
+        }
+        uint8_t* bh = smem + plan.op_offset + (size_t)sq * plan.op_bytes;
+#pragma unroll
+        for (int j = 0; j < kMaxBWords; ++j)
+          if (gt + j * kGroupThreads < b_words) {
+            uint4 h, l;
+            split_word(wb[j], h, l);
+            *reinterpret_cast<uint4*>(bh + 16 * (gt + j * kGroupThreads)) = h;
+            *reinterpret_cast<uint4*>(bh + plan.b_bytes + 16 * (gt + j * kGroupThreads)) = l;
+          }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&conv_full[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&op_full[sq]);
       }
     }
   } else if (warp == kTmaMmaWarp) {
@@ -452,14 +497,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
           const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            const int s = (int)(it % (uint32_t)stages);
-            if (!mbar_wait(&conv_full[s], (it / (uint32_t)stages) & 1u, abort_flag)) {
+            const uint32_t sq = it % Q;
+            if (!mbar_wait(&op_full[sq], (it / Q) & 1u, abort_flag)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = tmem_base + a_col0 + (uint32_t)s * kASlotCols, a_lo = a_hi + BK;
-            const uint32_t b_hi = smem_u32(smem + (size_t)s * plan.stage_bytes) + plan.a_bytes;
+            const uint32_t a_hi = tmem_base + a_col0 + sq * kASlotCols, a_lo = a_hi + BK;
+            const uint32_t b_hi = smem_u32(smem + plan.op_offset + (size_t)sq * plan.op_bytes);
             const uint32_t b_lo = b_hi + plan.b_bytes;
 #pragma unroll
             for (int j = 0; j < BK / 8; ++j) {
@@ -467,7 +512,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_lo, j), idesc, 1u);
               mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_hi, j), idesc, 1u);
             }
-            mma_commit(&empty[s]);
+            mma_commit(&op_empty[sq]);
           }
           mma_commit(&chunk_full[a]);
         }
