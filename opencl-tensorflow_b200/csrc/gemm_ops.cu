@@ -401,21 +401,33 @@ void tma_stages(int bn, bool use_s, int max_smem, int* raw_stages, int* op_stage
   *op_stages = q;
 }
 
-template <bool kAK, bool kBK>
+template <int AK, bool kBK>
 int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
                int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
   const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages);
   static int configured_bytes = 0;  // per instantiation
   if ((int)plan.total > configured_bytes) {
-    B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<kAK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<AK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)plan.total));
     configured_bytes = (int)plan.total;
   }
-  tma_gemm_kernel<kAK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, raw_stages, op_stages);
+  tma_gemm_kernel<AK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, raw_stages, op_stages);
   return check_launch(s, name);
 }
 
-int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N, int64_t K, float* out,
+// The A operand of a TMA-engine contraction: a plain matrix, or an im2col
+// view of an NHWC input whose rows the TMA stages (x, n_images, cr).
+struct ASpec {
+  AKind kind;
+  MatOperand mat;
+  const float* x;
+  int64_t n_images;
+  ConvRows cr;
+};
+
+inline ASpec a_matrix(const MatOperand& m) { return ASpec{m.k_major ? kAK : kAMN, m, nullptr, 0, ConvRows{}}; }
+
+int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int64_t K, float* out,
                  const float* bias, cudaStream_t s, const char* name, int min_kb_per_split) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
@@ -430,9 +442,19 @@ int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N,
   tma_stages(bn, use_s, d->max_smem_optin, &raw_stages, &op_stages);
   if (raw_stages < 2 || op_stages < 2)
     return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
-  TmaProblem prob{M, N, K, kps, splits, bn, bias, false, use_s};
+  TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4};
   CUtensorMap ma, mb, md;
-  B2_RETURN_IF_ERROR(encode_operand(&ma, a, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
+  if (a.kind == kAK || a.kind == kAMN) {
+    B2_RETURN_IF_ERROR(encode_operand(&ma, a.mat, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
+  } else {
+    const ConvRows& cr = a.cr;
+    const int64_t wc = (int64_t)cr.W * cr.Ci;
+    const cuuint64_t dims[3] = {(cuuint64_t)wc, (cuuint64_t)cr.H, (cuuint64_t)a.n_images};
+    const cuuint64_t strides[2] = {(cuuint64_t)wc * 4, (cuuint64_t)(wc * cr.H * 4)};
+    const cuuint32_t box[3] = {(cuuint32_t)wc, (cuuint32_t)cr.span, 1};
+    B2_RETURN_IF_ERROR(encode_map(&ma, a.x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+    prob.a_tx = (uint32_t)(wc * cr.span * 4);
+  }
   B2_RETURN_IF_ERROR(encode_operand(&mb, b, K, bn, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
   const cuuint32_t obox[3] = {32, 32, 1};
   Scratch part;
@@ -450,14 +472,52 @@ int run_tma_gemm(const MatOperand& a, const MatOperand& b, int64_t M, int64_t N,
   }
   const int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
   int rc;
-  if (a.k_major && b.k_major) rc = launch_tma<true, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
-  else if (a.k_major) rc = launch_tma<true, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
-  else if (b.k_major) rc = launch_tma<false, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
-  else rc = launch_tma<false, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+  switch (a.kind) {
+    case kAK:
+      rc = b.k_major ? launch_tma<kAK, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name)
+                     : launch_tma<kAK, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+      break;
+    case kAMN:
+      rc = b.k_major ? launch_tma<kAMN, true>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name)
+                     : launch_tma<kAMN, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+      break;
+    case kAFpropRows:
+      rc = launch_tma<kAFpropRows, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+      break;
+    default:
+      rc = launch_tma<kAWgradRows, false>(ma, mb, md, prob, raw_stages, op_stages, grid, s, name);
+      break;
+  }
   B2_RETURN_IF_ERROR(rc);
   if (splits == 1) return B2_OK;
   splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
   return check_launch(s, "splitk_reduce");
+}
+
+// Staged-row im2col A for a Conv2D forward (rows = output pixels,
+// rows_per_unit = BM) or filter gradient (k = output pixels, rows_per_unit =
+// BK): eligible when whole input rows fit one TMA box (W*Ci <= 256 floats,
+// 16-byte pitch), a tile / k-block never spans two images, and the staged
+// rows fit the 16 KB raw A area.
+bool conv_rows_spec(const ConvGeom& g, const float* x, int64_t pixels_per_unit, ASpec* a) {
+  const int64_t wc = g.W * g.Ci;
+  if (!tma_engine_enabled() || !aligned16(x) || wc <= 0 || wc > 256 || wc % 4 != 0 || g.Wo <= 0 ||
+      (g.Ho * g.Wo) % pixels_per_unit != 0 || g.H > kI32 || g.N > kI32)
+    return false;
+  const int64_t jmax = (g.Wo - 1 + pixels_per_unit - 1) / g.Wo + 1;
+  const int64_t span = (jmax - 1) * g.sH + g.kH;
+  if (span > 256 || span * wc * 4 > (int64_t)BM * BK * 4) return false;
+  a->kind = pixels_per_unit == BM ? kAFpropRows : kAWgradRows;
+  a->mat = MatOperand{nullptr, 0, 0, false};
+  a->x = x;
+  a->n_images = g.N;
+  a->cr = ConvRows{(int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW, (int)g.pH, (int)g.pW,
+                   (int)g.Ho, (int)g.Wo, (int)span};
+  return true;
+}
+
+bool tma_output_ok(const float* out, int64_t M, int64_t N) {
+  return aligned16(out) && N % 4 == 0 && M <= kI32 && N <= kI32;
 }
 
 template <class AV, class BV>
@@ -470,7 +530,7 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
     const MatOperand ma = mat_of(a), mb = mat_of(b);
     if (K > 0 && tma_engine_enabled() && tma_operand_ok(ma, K) && tma_operand_ok(mb, K) && aligned16(out) &&
         N % 4 == 0 && M <= kI32 && N <= kI32)
-      return run_tma_gemm(ma, mb, M, N, K, out, bias, s, name, min_kb_per_split);
+      return run_tma_gemm(a_matrix(ma), mb, M, N, K, out, bias, s, name, min_kb_per_split);
   }
   const int bn = choose_bn(N);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
@@ -562,6 +622,10 @@ int b2_conv2d(b2_stream_t stream, const float* input, const int64_t input_shape[
     const KContig av{input, M, g.Ci, aligned16(input) && g.Ci % 4 == 0};
     return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_forward");
   }
+  ASpec rows;
+  const MatOperand fb = mat_of(bv);
+  if (conv_rows_spec(g, input, BM, &rows) && tma_operand_ok(fb, K) && tma_output_ok(output, M, g.Co))
+    return run_tma_gemm(rows, fb, M, g.Co, K, output, nullptr, s, "conv2d_forward", 4);
   const ConvFpropA av{input, M, (int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW,
                       (int)g.pH, (int)g.pW, (int)g.Ho, (int)g.Wo, aligned16(input) && g.Ci % 4 == 0};
   return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_forward");
@@ -621,6 +685,10 @@ int b2_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int6
     const MNMajor av{input, g.Ci, g.Ci};
     return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_backprop_filter");
   }
+  ASpec rows;
+  const MatOperand gb = mat_of(bv);
+  if (conv_rows_spec(g, input, BK, &rows) && tma_operand_ok(gb, K) && tma_output_ok(output, M, g.Co))
+    return run_tma_gemm(rows, gb, M, g.Co, K, output, nullptr, s, "conv2d_backprop_filter", 4);
   const ConvWgradA av{input, M, (int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW,
                       (int)g.pH, (int)g.pW, (int)g.Ho, (int)g.Wo};
   return run_gemm(av, bv, M, g.Co, K, output, nullptr, s, "conv2d_backprop_filter");

@@ -73,7 +73,24 @@ constexpr uint32_t kEpiBuf = 32 * 128;  // one 32 x 32 fp32 output block
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kASlotCols = 2 * BK;  // A hi and lo of one k-block
 
+// How the A tile of a k-block is produced.
+enum AKind : int {
+  kAMN = 0,         // MN-major matrix: op(r, k) = p[k*ld + r]
+  kAK = 1,          // K-major matrix: op(r, k) = p[r*ld + k]
+  kAFpropRows = 2,  // Conv2D forward im2col: rows = output pixels, k = (kh, kw, ci)
+  kAWgradRows = 3,  // Conv2D filter-grad im2col^T: rows = (kh, kw, ci), k = output pixels
+};
+
+// NHWC input geometry for the im2col kinds.  The TMA stages `span` whole
+// input rows (W*Ci floats each, rows outside the image zero-filled) covering
+// every output row the k-block touches; the converters gather A from them.
+struct ConvRows {
+  int H, W, Ci, kW, sH, sW, pH, pW, Ho, Wo;
+  int span;  // input rows staged per k-block
+};
+
 struct TmaProblem {
+  ConvRows cr;
   int64_t M, N, K;
   int64_t k_per_split;  // multiple of BK
   int splits;
@@ -81,6 +98,7 @@ struct TmaProblem {
   const float* bias;  // per-column bias, direct mode only
   bool partial;       // out is [splits][M][N] partials (3-D store map)
   bool use_s;         // some tile spans several chunks: keep a running sum S
+  uint32_t a_tx;      // bytes of the raw A load per k-block (<= 16 KB)
 };
 
 // TMEM columns used by the accumulators (P0, P1 and, when needed, S).
@@ -132,6 +150,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -223,9 +250,9 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
       : "memory");
 }
 
-template <bool kAK>
+template <bool kKMajor>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int j) {
-  if constexpr (kAK) return smem_desc_swz(base + (uint32_t)j * 32u, 16u, 1024u, 2u);
+  if constexpr (kKMajor) return smem_desc_swz(base + (uint32_t)j * 32u, 16u, 1024u, 2u);
   else return smem_desc_swz(base + (uint32_t)j * 1024u, 4096u, 512u, 1u);
 }
 
@@ -267,32 +294,45 @@ __device__ __forceinline__ TmaTile tma_tile(const TmaProblem& p, int64_t t) {
   return c;
 }
 
-// Loads of one k-block (raw A tile 128 x 32, raw B tile BN x 32) into a raw
-// stage.
-template <bool kAK, bool kBK>
+// First output row (n * Ho + ho) of the pixels [p0, ...) and the input row
+// its staging starts at.
+__device__ __forceinline__ void staged_rows(const ConvRows& cr, int64_t p0, int* n, int* hi_first) {
+  const int ro = (int)(p0 / cr.Wo);
+  *n = ro / cr.Ho;
+  *hi_first = (ro - *n * cr.Ho) * cr.sH - cr.pH;
+}
+
+// Loads of one k-block (raw A: tile or staged input rows; raw B tile
+// BN x 32) into a raw stage.
+template <int AK, bool kBK>
 __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUtensorMap* map_b, uint32_t st,
-                                            uint32_t a_bytes, uint64_t* bar, uint32_t tx, const TmaTile& tc, int kb,
-                                            int bn) {
+                                            uint32_t a_bytes, uint64_t* bar, uint32_t tx, const TmaProblem& p,
+                                            const TmaTile& tc, int kb) {
   const uint32_t b_raw = st + a_bytes;
   const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
   mbar_expect_tx(bar, tx);
-  if constexpr (kAK) {
+  if constexpr (AK == kAK) {
     tma_load_2d(st, map_a, k0, (int)tc.m0, bar);
-  } else {
+  } else if constexpr (AK == kAMN) {
 #pragma unroll
     for (int b = 0; b < BM / 32; ++b) tma_load_2d(st + 4096u * b, map_a, (int)tc.m0 + 32 * b, k0, bar);
+  } else {
+    int n, hi_first;
+    staged_rows(p.cr, AK == kAFpropRows ? tc.m0 : (int64_t)k0, &n, &hi_first);
+    tma_load_3d(st, map_a, 0, hi_first, n, bar);
   }
   if constexpr (kBK) {
     tma_load_2d(b_raw, map_b, k0, (int)tc.n0, bar);
   } else {
-    for (int b = 0; b < bn / 32; ++b) tma_load_2d(b_raw + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
+    for (int b = 0; b < p.bn / 32; ++b) tma_load_2d(b_raw + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
   }
 }
 
-// Row r, k = 16h .. 16h+15 of a landed raw A tile.
-template <bool kAK>
-__device__ __forceinline__ void read_a_row(const uint8_t* raw, int r, int h, float (&v)[16]) {
-  if constexpr (kAK) {
+// Row r, k = k0 + 16h .. +15 of A, from a landed raw stage.
+template <int AK>
+__device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem& p, const TmaTile& tc, int k0,
+                                           int r, int h, float (&v)[16]) {
+  if constexpr (AK == kAK) {
     // [128 rows][128 B], 16-byte chunk j of row r at chunk position j ^ (r & 7)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -302,11 +342,57 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, int r, int h, flo
       v[4 * j + 2] = q.z;
       v[4 * j + 3] = q.w;
     }
-  } else {
+  } else if constexpr (AK == kAMN) {
     // [4 blocks][32 k][32 rows]
     const float* col = reinterpret_cast<const float*>(raw + (r >> 5) * 4096) + (r & 31);
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = col[(16 * h + i) * 32];
+  } else {
+    const ConvRows& cr = p.cr;
+    const float* xs = reinterpret_cast<const float*>(raw);  // [span][W * Ci]
+    const int wc = cr.W * cr.Ci;
+    const int64_t k = k0 + 16 * h;
+    if constexpr (AK == kAFpropRows) {
+      // row = output pixel m; k = (kh, kw, ci)
+      const int64_t m = tc.m0 + r;
+      const bool mok = m < p.M;
+      const int ro = (int)(m / cr.Wo), wo = (int)(m - (int64_t)ro * cr.Wo);
+      const int j = ro - (int)(tc.m0 / cr.Wo);
+      const int tap = (int)(k / cr.Ci);
+      int ci = (int)(k - (int64_t)tap * cr.Ci), kh = tap / cr.kW, kw = tap - kh * cr.kW;
+      const int wb = wo * cr.sW - cr.pW;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int wi = wb + kw;
+        v[i] = (mok && k + i < p.K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
+                                                                       : 0.0f;
+        if (++ci == cr.Ci) {
+          ci = 0;
+          if (++kw == cr.kW) {
+            kw = 0;
+            ++kh;
+          }
+        }
+      }
+    } else {
+      // row = filter element m = (kh, kw, ci); k = output pixel
+      const int m = (int)tc.m0 + r;
+      const bool mok = m < p.M;
+      const int tap = m / cr.Ci, ci = m - tap * cr.Ci, kh = tap / cr.kW, kw = tap - kh * cr.kW;
+      const int ro = (int)(k / cr.Wo);
+      int wo = (int)(k - (int64_t)ro * cr.Wo);
+      int j = ro - (int)((int64_t)k0 / cr.Wo);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int wi = wo * cr.sW - cr.pW + kw;
+        v[i] = (mok && k + i < p.K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
+                                                                       : 0.0f;
+        if (++wo == cr.Wo) {
+          wo = 0;
+          ++j;
+        }
+      }
+    }
   }
 }
 
@@ -321,7 +407,7 @@ __device__ __forceinline__ void split16(const float (&v)[16], uint32_t (&hv)[16]
 constexpr int kGroupThreads = 128;  // one converter group: a warp per TMEM lane quarter
 constexpr int kMaxBWords = kTmaMaxBN * BK * 4 / 16 / kGroupThreads;  // 16-byte B words per thread
 
-template <bool kAK, bool kBK>
+template <int AK, bool kBK>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     tma_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_d, const TmaProblem p, const int raw_stages,
@@ -346,7 +432,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int64_t tiles = nt * mt * p.splits;
   const uint32_t acc_cols = (uint32_t)bn;
   const uint32_t a_col0 = tma_acc_cols(bn, p.use_s);  // first A slot column
-  const uint32_t tx = plan.raw_bytes;
+  const uint32_t tx = p.a_tx + plan.b_bytes;  // bytes the TMA delivers per k-block
   const uint32_t R = (uint32_t)raw_stages, Q = (uint32_t)op_stages;
 
   // TMA issue cursor (lane 0 of warp 0): tile t, k-block kb, raw stage use it.
@@ -376,8 +462,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     // block-wide barrier so the loads overlap the TMEM allocation.
     if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
     while (t_iss < tiles && it_iss < R) {
-      issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)it_iss * plan.raw_bytes), plan.a_bytes,
-                            &raw_full[it_iss], tx, tc_iss, kb_iss, bn);
+      issue_stage<AK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)it_iss * plan.raw_bytes), plan.a_bytes,
+                           &raw_full[it_iss], tx, p, tc_iss, kb_iss);
       ++it_iss;
       if (++kb_iss == tc_iss.nkb) {
         kb_iss = 0;
@@ -403,8 +489,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       while (t_iss < tiles) {
         const uint32_t s = it_iss % R;
         if (!mbar_wait(&raw_empty[s], (it_iss / R - 1) & 1u, abort_flag)) break;
-        issue_stage<kAK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.raw_bytes), plan.a_bytes,
-                              &raw_full[s], tx, tc_iss, kb_iss, bn);
+        issue_stage<AK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.raw_bytes), plan.a_bytes,
+                             &raw_full[s], tx, p, tc_iss, kb_iss);
         ++it_iss;
         if (++kb_iss == tc_iss.nkb) {
           kb_iss = 0;
@@ -440,8 +526,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         }
         const uint8_t* raw = smem + (size_t)sr * plan.raw_bytes;
         float va[2][16];
-        read_a_row<kAK>(raw, row, 0, va[0]);
-        read_a_row<kAK>(raw, row, 1, va[1]);
+        const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
+        read_a_row<AK>(raw, p, tc, k0, row, 0, va[0]);
+        read_a_row<AK>(raw, p, tc, k0, row, 1, va[1]);
         uint4 wb[kMaxBWords];
 #pragma unroll
         for (int j = 0; j < kMaxBWords; ++j)

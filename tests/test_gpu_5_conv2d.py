@@ -52,6 +52,11 @@ SHAPES = [
     ((1, 1, 1, 1), (1, 1, 1, 1), (1, 1, 1, 1), "SAME"),
     ((3, 6, 6, 12), (2, 2, 12, 300), (1, 2, 2, 1), "SAME"),     # N > 256: several N tiles
     ((2, 7, 7, 16), (3, 3, 16, 16), (1, 1, 1, 1), "VALID"),
+    # staged-row im2col path of the TMA engine (whole input rows <= 256 floats)
+    ((2, 16, 16, 4), (3, 3, 4, 40), (1, 1, 1, 1), "SAME"),
+    ((2, 32, 16, 4), (5, 5, 4, 24), (1, 2, 2, 1), "SAME"),
+    ((2, 33, 17, 4), (3, 3, 4, 20), (1, 2, 2, 1), "VALID"),
+    ((4, 32, 32, 3), (3, 3, 3, 36), (1, 1, 1, 1), "SAME"),
 ]
 
 
