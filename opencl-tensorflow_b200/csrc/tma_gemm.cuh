@@ -1,42 +1,48 @@
-// tma_gemm.cuh -- 3xTF32 GEMM engine fed by the Tensor Memory Accelerator,
-// for contractions whose operands are plain row-major matrices (Dense forward
-// and backward, 1x1 / stride-1 / unpadded Conv2D forward and gradients).
+// tma_gemm.cuh -- 3xTF32 GEMM engine fed by the Tensor Memory Accelerator.
 //
-// D[M,N] = sum_k A[m,k] B[k,n].  Each operand is K-major (op(r, k) =
-// p[r*ld + k]) or MN-major (op(r, k) = p[k*ld + r]).  Per 32-wide k-block:
+// D[M,N] = sum_k A[m,k] B[k,n] for Dense forward / backward, 1x1 Conv2D and
+// the Conv2D forward / filter gradient of inputs with short rows (the README
+// stem).  Per 32-wide k-block:
 //
-//   A  TMA loads the raw fp32 tile (K-major: one box {32, 128} with the
-//      128-byte swizzle, so the converters' row reads are conflict-free;
-//      MN-major: four boxes {32 rows, 32 k}, unswizzled).  The converter
-//      warps split each element x -> hi = tf32(x), lo = tf32(x - hi) and
-//      write both into a tensor-memory slot (128 lanes = rows, 32 + 32
-//      columns), where the MMA reads A.  A never returns to shared memory,
-//      so the three MMAs of a k step read only B from it.
-//   B  TMA loads the tile in the layout UMMA reads in place (K-major: box
+//   A  TMA loads raw fp32 data into a raw stage: a K-major matrix tile (one
+//      box {32, 128}, 128-byte swizzle, so the converters' row reads are
+//      conflict-free), an MN-major tile (four unswizzled boxes {32 rows,
+//      32 k}), or, for the im2col kinds, every NHWC input row the k-block
+//      touches (one box of whole rows, zero-filled outside the image).  The
+//      converter warps read their row of A (gathering im2col elements from
+//      the staged rows), split each element into x = hi + lo (tf32_hi_bits)
+//      and write both into a tensor-memory slot (128 lanes = rows, 32 + 32
+//      columns) from which the MMA reads A.
+//   B  TMA loads the tile in a layout UMMA reads directly (K-major: box
 //      {32, BN}, 128-byte swizzle, SBO = 1024 B, k step +32 B; MN-major: BN/32
 //      boxes {32, 32} with the 128-byte swizzle of 32-byte atoms, the only
 //      MN-major smem layout tf32 UMMA accepts, LBO = 4096 B, SBO = 512 B,
-//      k step +1024 B); the converters split it in place (hi where x was, lo
-//      at the same offset of the stage's lo tile, so the swizzle carries over).
+//      k step +1024 B); the converters write hi and lo at the same offsets
+//      of an operand stage, so the swizzle carries over.
 //
 // Out-of-range rows and k are zero-filled by the TMA unit.  One CTA per SM
 // loops over output tiles 128 x BN (BN a multiple of 32, <= 96) and split-K
-// slices, with four warp roles:
+// slices.  Two rings decouple the memory latency from the tensor work: raw
+// stages (TMA -> converters) and operand stages (converters -> MMA: B hi/lo
+// in shared memory, A hi/lo in TMEM).  Warp roles:
 //
-//   warp 0       lane 0 waits for a free stage (EMPTY), posts the stage's
+//   warp 0       lane 0 waits for a free raw stage (RAW_EMPTY), posts its
 //                byte count on RAW_FULL and issues the TMA loads; the first
-//                round of stages is issued before the block-wide barrier.
+//                round is issued before the block-wide barrier, overlapping
+//                the TMEM allocation.
 //   warp 1       allocates all 512 TMEM columns: chunk accumulators P0, P1,
 //                the running sum S (only when a tile spans several chunks)
-//                and one A slot per stage.  Lane 0 waits CONV_FULL and issues,
-//                per 8-wide k step, P += Alo*Bhi + Ahi*Blo + Ahi*Bhi
+//                and one A slot per operand stage.  Lane 0 waits OP_FULL and
+//                issues, per 8-wide k step, P += Alo*Bhi + Ahi*Blo + Ahi*Bhi
 //                (tcgen05.mma kind::tf32, A from TMEM, B from shared memory),
-//                commits EMPTY per stage and CHUNK_FULL per chunk (at most
-//                kChunkKB k-blocks).
-//   warps 2-9    converters (two per TMEM lane quarter, 16 k each): wait
-//                RAW_FULL, split their row of A into the TMEM slot
-//                (tcgen05.st), split B in place (integer round-to-nearest),
-//                fence both proxies, arrive CONV_FULL.
+//                commits OP_EMPTY per operand stage and CHUNK_FULL per chunk
+//                (at most kChunkKB k-blocks).
+//   warps 2-9    converters, two groups of four warps (one per TMEM lane
+//                quarter) on alternate k-blocks: wait RAW_FULL, read their
+//                row of A and a share of B, release the raw stage, wait for a
+//                free operand stage, write A into its TMEM slot (tcgen05.st)
+//                and B hi / lo into its shared-memory tiles, fence both
+//                proxies, arrive OP_FULL.
 //   warps 10-13  epilogue: per chunk fold P into S with round-to-nearest fp32
 //                adds; after the tile's last chunk, add the bias, write the
 //                warp's 32 x BN block as 128-byte-swizzled 32 x 32 pieces into
@@ -199,23 +205,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Round an fp32 bit pattern to tf32 (10 explicit mantissa bits), to nearest
-// with ties away from zero: add half a tf32 ulp to the magnitude and clear the
-// 13 dropped bits.  Inf and NaN pass through unchanged.
-__device__ __forceinline__ uint32_t tf32_round_bits(uint32_t u) {
+// 3xTF32 operand split: x = hi + lo with hi = tf32(x) rounded to nearest
+// (ties away from zero: add half a tf32 ulp to the magnitude, clear the 13
+// dropped bits; Inf and NaN pass through) and lo = x - hi, exact in fp32.
+// The tensor core reads the top 19 bits of each element, so lo enters
+// truncated to tf32; since lo has either sign that error is unbiased, and
+// hi + lo carries x to within 2^-21 |x| (typically ~2^-23).
+__device__ __forceinline__ uint32_t tf32_hi_bits(uint32_t u) {
   return (u & 0x7F800000u) == 0x7F800000u ? u : ((u + 0x1000u) & 0xFFFFE000u);
 }
 
-// x -> (hi, lo): hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32).
+__device__ __forceinline__ uint32_t tf32_lo_bits(uint32_t u, uint32_t hi) {
+  return __float_as_uint(__uint_as_float(u) - __uint_as_float(hi));
+}
+
 __device__ __forceinline__ void split_word(uint4 w, uint4& h, uint4& l) {
-  h.x = tf32_round_bits(w.x);
-  h.y = tf32_round_bits(w.y);
-  h.z = tf32_round_bits(w.z);
-  h.w = tf32_round_bits(w.w);
-  l.x = tf32_round_bits(__float_as_uint(__uint_as_float(w.x) - __uint_as_float(h.x)));
-  l.y = tf32_round_bits(__float_as_uint(__uint_as_float(w.y) - __uint_as_float(h.y)));
-  l.z = tf32_round_bits(__float_as_uint(__uint_as_float(w.z) - __uint_as_float(h.z)));
-  l.w = tf32_round_bits(__float_as_uint(__uint_as_float(w.w) - __uint_as_float(h.w)));
+  h.x = tf32_hi_bits(w.x);
+  h.y = tf32_hi_bits(w.y);
+  h.z = tf32_hi_bits(w.z);
+  h.w = tf32_hi_bits(w.w);
+  l.x = tf32_lo_bits(w.x, h.x);
+  l.y = tf32_lo_bits(w.y, h.y);
+  l.z = tf32_lo_bits(w.z, h.z);
+  l.w = tf32_lo_bits(w.w, h.w);
 }
 
 // UMMA shared-memory descriptor with a swizzled layout: type 2 = 128-byte
@@ -351,21 +363,22 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
     const ConvRows& cr = p.cr;
     const float* xs = reinterpret_cast<const float*>(raw);  // [span][W * Ci]
     const int wc = cr.W * cr.Ci;
-    const int64_t k = k0 + 16 * h;
+    const int K = (int)p.K;  // M, K < 2^31 on this path (checked on the host)
+    const int k = k0 + 16 * h;
     if constexpr (AK == kAFpropRows) {
       // row = output pixel m; k = (kh, kw, ci)
-      const int64_t m = tc.m0 + r;
-      const bool mok = m < p.M;
-      const int ro = (int)(m / cr.Wo), wo = (int)(m - (int64_t)ro * cr.Wo);
-      const int j = ro - (int)(tc.m0 / cr.Wo);
-      const int tap = (int)(k / cr.Ci);
-      int ci = (int)(k - (int64_t)tap * cr.Ci), kh = tap / cr.kW, kw = tap - kh * cr.kW;
+      const int m = (int)tc.m0 + r;
+      const bool mok = m < (int)p.M;
+      const int ro = m / cr.Wo, wo = m - ro * cr.Wo;
+      const int j = ro - (int)tc.m0 / cr.Wo;
+      const int tap = k / cr.Ci;
+      int ci = k - tap * cr.Ci, kh = tap / cr.kW, kw = tap - kh * cr.kW;
       const int wb = wo * cr.sW - cr.pW;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int wi = wb + kw;
-        v[i] = (mok && k + i < p.K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
-                                                                       : 0.0f;
+        v[i] = (mok && k + i < K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
+                                                                     : 0.0f;
         if (++ci == cr.Ci) {
           ci = 0;
           if (++kw == cr.kW) {
@@ -377,16 +390,16 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
     } else {
       // row = filter element m = (kh, kw, ci); k = output pixel
       const int m = (int)tc.m0 + r;
-      const bool mok = m < p.M;
+      const bool mok = m < (int)p.M;
       const int tap = m / cr.Ci, ci = m - tap * cr.Ci, kh = tap / cr.kW, kw = tap - kh * cr.kW;
-      const int ro = (int)(k / cr.Wo);
-      int wo = (int)(k - (int64_t)ro * cr.Wo);
-      int j = ro - (int)((int64_t)k0 / cr.Wo);
+      const int ro = k / cr.Wo;
+      int wo = k - ro * cr.Wo;
+      int j = ro - k0 / cr.Wo;
+      const float* xrow = xs + kh * wc + ci;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int wi = wo * cr.sW - cr.pW + kw;
-        v[i] = (mok && k + i < p.K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
-                                                                       : 0.0f;
+        v[i] = (mok && k + i < K && (unsigned)wi < (unsigned)cr.W) ? xrow[j * cr.sH * wc + wi * cr.Ci] : 0.0f;
         if (++wo == cr.Wo) {
           wo = 0;
           ++j;
@@ -399,8 +412,8 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
 __device__ __forceinline__ void split16(const float (&v)[16], uint32_t (&hv)[16], uint32_t (&lv)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    hv[i] = tf32_round_bits(__float_as_uint(v[i]));
-    lv[i] = tf32_round_bits(__float_as_uint(v[i] - __uint_as_float(hv[i])));
+    hv[i] = tf32_hi_bits(__float_as_uint(v[i]));
+    lv[i] = tf32_lo_bits(__float_as_uint(v[i]), hv[i]);
   }
 }
 
