@@ -391,10 +391,10 @@ int tma_bn(int64_t N) {
 
 // Operand stages: limited by the TMEM columns left for A slots; raw stages
 // take the remaining shared memory.
-void tma_stages(int bn, bool use_s, int max_smem, int* raw_stages, int* op_stages) {
+void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_stages, int* op_stages) {
   int q = (int)((kTmemCols - tma_acc_cols(bn, use_s)) / kASlotCols);
   if (q > kTmaMaxOpStages) q = kTmaMaxOpStages;
-  const TmaSmem fixed = tma_smem_plan(bn, 0, q);
+  const TmaSmem fixed = tma_smem_plan(bn, 0, q, table_entries);
   int r = (int)((max_smem - (int)fixed.total) / (int)fixed.raw_bytes);
   if (r > kTmaMaxStages) r = kTmaMaxStages;
   *raw_stages = r;
@@ -404,7 +404,7 @@ void tma_stages(int bn, bool use_s, int max_smem, int* raw_stages, int* op_stage
 template <int AK, bool kBK>
 int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
                int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
-  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages);
+  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? (int)prob.K : 0);
   static int configured_bytes = 0;  // per instantiation
   if ((int)plan.total > configured_bytes) {
     B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<AK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -439,7 +439,7 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   splits = (int)ceil_div(K, kps);
   const bool use_s = kps > (int64_t)kChunkKB * BK;
   int raw_stages = 0, op_stages = 0;
-  tma_stages(bn, use_s, d->max_smem_optin, &raw_stages, &op_stages);
+  tma_stages(bn, use_s, a.kind == kAFpropRows ? (int)K : 0, d->max_smem_optin, &raw_stages, &op_stages);
   if (raw_stages < 2 || op_stages < 2)
     return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
   TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4};
@@ -451,9 +451,9 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
     const int64_t wc = (int64_t)cr.W * cr.Ci;
     const cuuint64_t dims[3] = {(cuuint64_t)wc, (cuuint64_t)cr.H, (cuuint64_t)a.n_images};
     const cuuint64_t strides[2] = {(cuuint64_t)wc * 4, (cuuint64_t)(wc * cr.H * 4)};
-    const cuuint32_t box[3] = {(cuuint32_t)wc, (cuuint32_t)cr.span, 1};
+    const cuuint32_t box[3] = {(cuuint32_t)cr.wcp, (cuuint32_t)cr.span, 1};
     B2_RETURN_IF_ERROR(encode_map(&ma, a.x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
-    prob.a_tx = (uint32_t)(wc * cr.span * 4);
+    prob.a_tx = (uint32_t)(cr.wcp * cr.span * 4);
   }
   B2_RETURN_IF_ERROR(encode_operand(&mb, b, K, bn, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
   const cuuint32_t obox[3] = {32, 32, 1};
@@ -501,18 +501,23 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
 // rows fit the 16 KB raw A area.
 bool conv_rows_spec(const ConvGeom& g, const float* x, int64_t pixels_per_unit, ASpec* a) {
   const int64_t wc = g.W * g.Ci;
-  if (!tma_engine_enabled() || !aligned16(x) || wc <= 0 || wc > 256 || wc % 4 != 0 || g.Wo <= 0 ||
+  if (!tma_engine_enabled() || !aligned16(x) || wc <= 0 || wc % 4 != 0 || g.Wo <= 0 ||
       (g.Ho * g.Wo) % pixels_per_unit != 0 || g.H > kI32 || g.N > kI32)
     return false;
   const int64_t jmax = (g.Wo - 1 + pixels_per_unit - 1) / g.Wo + 1;
   const int64_t span = (jmax - 1) * g.sH + g.kH;
-  if (span > 256 || span * wc * 4 > (int64_t)BM * BK * 4) return false;
+  // staged row: xpad zeros, the W*Ci values, zeros up to the last tap's column
+  const int64_t xpad = ceil_div(g.pW * g.Ci, 4) * 4;
+  const int64_t last_col = ((g.Wo - 1) * g.sW - g.pW + g.kW) * g.Ci;  // one past the last tap read
+  const int64_t wcp = ceil_div(xpad + (last_col > wc ? last_col : wc), 4) * 4;
+  if (wcp > 256 || span > 256 || span * wcp * 4 > (int64_t)BM * BK * 4) return false;
+  if (pixels_per_unit == BM && g.kH * g.kW * g.Ci > kMaxImTable) return false;
   a->kind = pixels_per_unit == BM ? kAFpropRows : kAWgradRows;
   a->mat = MatOperand{nullptr, 0, 0, false};
   a->x = x;
   a->n_images = g.N;
   a->cr = ConvRows{(int)g.H, (int)g.W, (int)g.Ci, (int)g.kW, (int)g.sH, (int)g.sW, (int)g.pH, (int)g.pW,
-                   (int)g.Ho, (int)g.Wo, (int)span};
+                   (int)g.Ho, (int)g.Wo, (int)span, (int)xpad, (int)wcp};
   return true;
 }
 

@@ -87,12 +87,17 @@ enum AKind : int {
   kAWgradRows = 3,  // Conv2D filter-grad im2col^T: rows = (kh, kw, ci), k = output pixels
 };
 
-// NHWC input geometry for the im2col kinds.  The TMA stages `span` whole
-// input rows (W*Ci floats each, rows outside the image zero-filled) covering
-// every output row the k-block touches; the converters gather A from them.
+// NHWC input geometry for the im2col kinds.  The TMA stages `span` input
+// rows covering every output row the k-block touches, each widened to `wcp`
+// floats: `xpad` zeros (>= pW*Ci, a multiple of 4) before the row's W*Ci
+// values and zeros after them past the right padding, so that every tap of
+// every output pixel lands inside the staged row and the converters gather
+// without bounds checks; rows outside the image are zero-filled too.
 struct ConvRows {
   int H, W, Ci, kW, sH, sW, pH, pW, Ho, Wo;
   int span;  // input rows staged per k-block
+  int xpad;  // zeros staged before each row (floats)
+  int wcp;   // staged row width (floats, multiple of 4, <= 256)
 };
 
 struct TmaProblem {
@@ -112,13 +117,17 @@ __host__ __device__ inline uint32_t tma_acc_cols(int bn, bool use_s) { return (u
 
 struct TmaSmem {
   int raw_stages, op_stages;
-  uint32_t a_bytes, b_bytes, raw_bytes, op_bytes, op_offset, epi_offset, bar_offset, total;
+  uint32_t a_bytes, b_bytes, raw_bytes, op_bytes, op_offset, epi_offset, bar_offset, table_offset, total;
 };
+
+// Conv2D-forward im2col: staged-row offset of each k = (kh, kw, ci), one int
+// per k, at most this many (K = kH*kW*Ci).
+constexpr int kMaxImTable = 1024;
 
 // Shared memory: a ring of raw stages (TMA destinations: raw A tile + raw B
 // tile), a ring of operand stages (B hi tile + B lo tile, read by the MMA),
 // the epilogue buffers and the barriers.
-__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_stages) {
+__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_stages, int table_entries) {
   TmaSmem s;
   s.raw_stages = raw_stages;
   s.op_stages = op_stages;
@@ -129,7 +138,8 @@ __host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_
   s.op_offset = s.raw_bytes * (uint32_t)raw_stages;
   s.epi_offset = s.op_offset + s.op_bytes * (uint32_t)op_stages;
   s.bar_offset = s.epi_offset + 4 * (uint32_t)(bn / 32) * kEpiBuf;  // a 32 x BN block per epilogue warp
-  s.total = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4) + 16 + 1024;  // + alignment slack
+  s.table_offset = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4) + 16;
+  s.total = s.table_offset + 4 * (uint32_t)table_entries + 1024;  // + alignment slack
   return s;
 }
 
@@ -331,7 +341,7 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
   } else {
     int n, hi_first;
     staged_rows(p.cr, AK == kAFpropRows ? tc.m0 : (int64_t)k0, &n, &hi_first);
-    tma_load_3d(st, map_a, 0, hi_first, n, bar);
+    tma_load_3d(st, map_a, -p.cr.xpad, hi_first, n, bar);
   }
   if constexpr (kBK) {
     tma_load_2d(b_raw, map_b, k0, (int)tc.n0, bar);
@@ -343,7 +353,7 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
 // Row r, k = k0 + 16h .. +15 of A, from a landed raw stage.
 template <int AK>
 __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem& p, const TmaTile& tc, int k0,
-                                           int r, int h, float (&v)[16]) {
+                                           int r, int h, const int* imtab, float (&v)[16]) {
   if constexpr (AK == kAK) {
     // [128 rows][128 B], 16-byte chunk j of row r at chunk position j ^ (r & 7)
 #pragma unroll
@@ -361,48 +371,40 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
     for (int i = 0; i < 16; ++i) v[i] = col[(16 * h + i) * 32];
   } else {
     const ConvRows& cr = p.cr;
-    const float* xs = reinterpret_cast<const float*>(raw);  // [span][W * Ci]
-    const int wc = cr.W * cr.Ci;
+    const float* xs = reinterpret_cast<const float*>(raw);  // [span][wcp], column c at c + xpad
     const int K = (int)p.K;  // M, K < 2^31 on this path (checked on the host)
     const int k = k0 + 16 * h;
+    const int kwc = cr.kW * cr.Ci;
     if constexpr (AK == kAFpropRows) {
-      // row = output pixel m; k = (kh, kw, ci)
+      // imtab[k] = kh * wcp + kw * Ci + ci (filled at kernel start)
+      // row = output pixel m; k = (kh, kw, ci) at staged offset kh*wcp + kw*Ci + ci
+      // from the pixel's base (rows m >= M read in-bounds values and are never stored)
       const int m = (int)tc.m0 + r;
-      const bool mok = m < (int)p.M;
       const int ro = m / cr.Wo, wo = m - ro * cr.Wo;
       const int j = ro - (int)tc.m0 / cr.Wo;
-      const int tap = k / cr.Ci;
-      int ci = k - tap * cr.Ci, kh = tap / cr.kW, kw = tap - kh * cr.kW;
-      const int wb = wo * cr.sW - cr.pW;
+      const float* base = xs + j * cr.sH * cr.wcp + wo * cr.sW * cr.Ci + (cr.xpad - cr.pW * cr.Ci);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int wi = wb + kw;
-        v[i] = (mok && k + i < K && (unsigned)wi < (unsigned)cr.W) ? xs[(j * cr.sH + kh) * wc + wi * cr.Ci + ci]
-                                                                     : 0.0f;
-        if (++ci == cr.Ci) {
-          ci = 0;
-          if (++kw == cr.kW) {
-            kw = 0;
-            ++kh;
-          }
-        }
-      }
+      for (int i = 0; i < 16; ++i) v[i] = k + i < K ? base[imtab[k + i]] : 0.0f;
     } else {
-      // row = filter element m = (kh, kw, ci); k = output pixel
+      // row = filter element m = (kh, kw, ci); k = output pixel (j, wo) at
+      // staged offset j*sH*wcp + wo*sW*Ci from the element's base (K is a
+      // multiple of 32 on this path)
       const int m = (int)tc.m0 + r;
       const bool mok = m < (int)p.M;
-      const int tap = m / cr.Ci, ci = m - tap * cr.Ci, kh = tap / cr.kW, kw = tap - kh * cr.kW;
+      const int kh = m / kwc, kwci = m - kh * kwc;
+      const float* base = xs + kh * cr.wcp + kwci + (cr.xpad - cr.pW * cr.Ci);
       const int ro = k / cr.Wo;
       int wo = k - ro * cr.Wo;
-      int j = ro - k0 / cr.Wo;
-      const float* xrow = xs + kh * wc + ci;
+      int b = (ro - k0 / cr.Wo) * cr.sH * cr.wcp + wo * cr.sW * cr.Ci;
+      const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int wi = wo * cr.sW - cr.pW + kw;
-        v[i] = (mok && k + i < K && (unsigned)wi < (unsigned)cr.W) ? xrow[j * cr.sH * wc + wi * cr.Ci] : 0.0f;
+        v[i] = mok ? base[b] : 0.0f;
         if (++wo == cr.Wo) {
           wo = 0;
-          ++j;
+          b += wrap;
+        } else {
+          b += step;
         }
       }
     }
@@ -428,7 +430,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
-  const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages);
+  const int table_entries = AK == kAFpropRows ? (int)p.K : 0;
+  const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages, table_entries);
+  int* imtab = reinterpret_cast<int*>(smem + plan.table_offset);
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + plan.bar_offset);
   uint64_t* raw_empty = raw_full + kTmaMaxStages;
   uint64_t* op_full = raw_empty + kTmaMaxStages;
@@ -485,6 +489,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       }
     }
   }
+  if constexpr (AK == kAFpropRows) {
+    const int kwc = p.cr.kW * p.cr.Ci;
+    for (int k = threadIdx.x; k < table_entries; k += blockDim.x) imtab[k] = (k / kwc) * p.cr.wcp + k % kwc;
+  }
   if (warp == kTmaMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
@@ -540,8 +548,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const uint8_t* raw = smem + (size_t)sr * plan.raw_bytes;
         float va[2][16];
         const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
-        read_a_row<AK>(raw, p, tc, k0, row, 0, va[0]);
-        read_a_row<AK>(raw, p, tc, k0, row, 1, va[1]);
+        read_a_row<AK>(raw, p, tc, k0, row, 0, imtab, va[0]);
+        read_a_row<AK>(raw, p, tc, k0, row, 1, imtab, va[1]);
         uint4 wb[kMaxBWords];
 #pragma unroll
         for (int j = 0; j < kMaxBWords; ++j)
