@@ -211,6 +211,20 @@ int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* x,
                                     float epsilon, float* y, float* saved_mean,
                                     float* saved_var);
 
+/* The Keras layer's moving-statistics update after a training step,
+ * opencl_tf/layers.py:189-194: for c < channels,
+ *   moving_mean[c] = momentum * moving_mean[c] + one_minus_momentum * batch_mean[c]
+ *   moving_var[c]  = momentum * moving_var[c]  + one_minus_momentum * batch_var[c]
+ * with both products and the sum rounded to fp32 (the reference's three
+ * tensor ops).  one_minus_momentum is passed as the caller rounds 1 -
+ * momentum (the reference: in double, then to fp32).  Not an op of the
+ * reference's kernel library: it fuses the four elementwise ops the layer
+ * runs into one launch. */
+int b2_batch_norm_update_moving(b2_stream_t stream, float* moving_mean,
+                                float* moving_var, const float* batch_mean,
+                                const float* batch_var, int64_t channels,
+                                float momentum, float one_minus_momentum);
+
 /* OpenclBatchNormInference(x, gamma, beta, mean, var; epsilon) -> y
  * src/ops/batchnorm_ops.cc:192-282 */
 int b2_batch_norm_inference(b2_stream_t stream, const float* x,

@@ -194,31 +194,58 @@ __global__ void __launch_bounds__(kThreads)
 
 // Stage 2 for the statistics: saved_mean, saved_var (biased, E[x^2]-mean^2 as
 // batchnorm_kernels.cl:57-59) and the constants of the normalize pass.
-__global__ void bn_stats_finalize_kernel(const float2* __restrict__ partial, int blocks, int C, int64_t nhw,
-                                         float eps, float* __restrict__ mean, float* __restrict__ var,
-                                         float* __restrict__ inv_std) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= C) return;
+// Sum of the partials of channel c over all row blocks, in a fixed order:
+// thread t adds blocks t, t + kFinThreads, ... in order, then the CTA adds the
+// thread sums in a fixed pairwise tree.  One CTA of kFinThreads per channel.
+constexpr int kFinThreads = 128;
+__device__ __forceinline__ float2 sum_partials(const float2* __restrict__ partial, int blocks, int C, int c) {
+  __shared__ float2 s_red[kFinThreads];
   float a = 0.0f, b = 0.0f;
-  for (int i = lane; i < blocks; i += 32) {
-    const float2 p = partial[(int64_t)i * C + warp];
+#pragma unroll 4
+  for (int i = threadIdx.x; i < blocks; i += kFinThreads) {
+    const float2 p = partial[(int64_t)i * C + c];
     a += p.x;
     b += p.y;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
+  s_red[threadIdx.x] = make_float2(a, b);
+  __syncthreads();
+  for (int h = kFinThreads / 2; h > 0; h >>= 1) {
+    if ((int)threadIdx.x < h) {
+      const float2 o = s_red[threadIdx.x + h];
+      s_red[threadIdx.x].x += o.x;
+      s_red[threadIdx.x].y += o.y;
+    }
+    __syncthreads();
   }
-  if (lane == 0) {
+  return s_red[0];
+}
+
+// Stage 2 of the statistics: mean = sum / NHW, var = sum_sq / NHW - mean^2
+// (the reference's formula), inv_std = 1 / sqrt(var + eps).
+__global__ void __launch_bounds__(kFinThreads) bn_stats_finalize_kernel(const float2* __restrict__ partial,
+                                                                        int blocks, int C, int64_t nhw, float eps,
+                                                                        float* __restrict__ mean,
+                                                                        float* __restrict__ var,
+                                                                        float* __restrict__ inv_std) {
+  const int c = blockIdx.x;
+  const float2 s = sum_partials(partial, blocks, C, c);
+  if (threadIdx.x == 0) {
     const float n = (float)(int)nhw;  // the reference divides by (float)(int)NHW
-    const float m = __fdiv_rn(a, n);
-    const float v = __fsub_rn(__fdiv_rn(b, n), __fmul_rn(m, m));
-    mean[warp] = m;
-    var[warp] = v;
-    inv_std[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v, eps)));
+    const float m = __fdiv_rn(s.x, n);
+    const float v = __fsub_rn(__fdiv_rn(s.y, n), __fmul_rn(m, m));
+    mean[c] = m;
+    var[c] = v;
+    inv_std[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v, eps)));
   }
+}
+
+__global__ void bn_moving_update_kernel(float* __restrict__ mm, float* __restrict__ mv,
+                                        const float* __restrict__ bm, const float* __restrict__ bv, int C,
+                                        float momentum, float one_minus_momentum) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  mm[c] = __fadd_rn(__fmul_rn(momentum, mm[c]), __fmul_rn(one_minus_momentum, bm[c]));
+  mv[c] = __fadd_rn(__fmul_rn(momentum, mv[c]), __fmul_rn(one_minus_momentum, bv[c]));
 }
 
 // inv_std for the inference op (batchnorm_kernels.cl:78).
@@ -296,31 +323,19 @@ __global__ void __launch_bounds__(kThreads)
 
 // Stage 2 of the gradient: grad_beta = sum dy, grad_gamma = sum dy * x_hat;
 // also k1 = gamma * inv_std / NHW and inv_std for the dx pass.
-__global__ void bn_grad_finalize_kernel(const float2* __restrict__ partial, int blocks, int C, int64_t nhw,
-                                        float eps, const float* __restrict__ gamma, const float* __restrict__ var,
-                                        float* __restrict__ grad_beta, float* __restrict__ grad_gamma,
-                                        float* __restrict__ k1, float* __restrict__ inv_std) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= C) return;
-  float a = 0.0f, b = 0.0f;
-  for (int i = lane; i < blocks; i += 32) {
-    const float2 p = partial[(int64_t)i * C + warp];
-    a += p.x;
-    b += p.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
-  }
-  if (lane == 0) {
-    grad_beta[warp] = a;
-    grad_gamma[warp] = b;
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[warp], eps)));
+__global__ void __launch_bounds__(kFinThreads) bn_grad_finalize_kernel(
+    const float2* __restrict__ partial, int blocks, int C, int64_t nhw, float eps, const float* __restrict__ gamma,
+    const float* __restrict__ var, float* __restrict__ grad_beta, float* __restrict__ grad_gamma,
+    float* __restrict__ k1, float* __restrict__ inv_std) {
+  const int c = blockIdx.x;
+  const float2 s = sum_partials(partial, blocks, C, c);
+  if (threadIdx.x == 0) {
+    grad_beta[c] = s.x;
+    grad_gamma[c] = s.y;
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[c], eps)));
     const float n = (float)(int)nhw;
-    inv_std[warp] = inv;
-    k1[warp] = __fdiv_rn(__fmul_rn(gamma[warp], inv), n);
+    inv_std[c] = inv;
+    k1[c] = __fdiv_rn(__fmul_rn(gamma[c], inv), n);
   }
 }
 
@@ -460,7 +475,7 @@ int b2_batch_norm_training(b2_stream_t stream, const float* x, const int64_t x_s
   int used_blocks = 0;
   B2_RETURN_IF_ERROR(launch_partials(s, 0, x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, vec_ok, d,
                                      part.as<float2>(), &used_blocks));
-  bn_stats_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+  bn_stats_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
                                                                        epsilon, saved_mean, saved_var,
                                                                        inv.as<float>());
   B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
@@ -517,7 +532,7 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t gr
   int used_blocks = 0;
   B2_RETURN_IF_ERROR(launch_partials(s, 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C, vec_ok, d,
                                      part.as<float2>(), &used_blocks));
-  bn_grad_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+  bn_grad_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
                                                                       epsilon, gamma, saved_var, grad_beta,
                                                                       grad_gamma, k1, inv);
   B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
@@ -532,6 +547,23 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t gr
                                                    rows, (int)C, nhw_f, geo);
   }
   return check_launch(s, "bn_backward_dx");
+}
+
+// opencl_tf/layers.py:189-194 (the Keras layer's moving statistics):
+// moving = momentum * moving + (1 - momentum) * batch for mean and variance,
+// each product and the sum rounded to fp32 as the reference's three tensor ops
+// are.  One launch for both buffers.
+int b2_batch_norm_update_moving(b2_stream_t stream, float* moving_mean, float* moving_var, const float* batch_mean,
+                                const float* batch_var, int64_t channels, float momentum,
+                                float one_minus_momentum) {
+  clear_error();
+  B2_REQUIRE(channels >= 0 && channels <= kMaxInt32, "channels must be in [0, 2^31)");
+  if (channels == 0) return B2_OK;
+  B2_REQUIRE(moving_mean && moving_var && batch_mean && batch_var, "null buffer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bn_moving_update_kernel<<<(unsigned)ceil_div(channels, 256), 256, 0, s>>>(
+      moving_mean, moving_var, batch_mean, batch_var, (int)channels, momentum, one_minus_momentum);
+  return check_launch(s, "bn_update_moving");
 }
 
 }  // extern "C"
@@ -616,7 +648,7 @@ extern "C" int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* 
     bn_partial_kernel<1, 0><<<grid, kThreads, 0, s>>>(x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, geo,
                                                         partial);
   B2_RETURN_IF_ERROR(check_launch(s, "bn_reduce_stats (no alloc)"));
-  bn_stats_finalize_kernel<<<(int)ceil_div(C * 32, 256), 256, 0, s>>>(partial, blocks, (int)C, rows, epsilon,
+  bn_stats_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(partial, blocks, (int)C, rows, epsilon,
                                                                        saved_mean, saved_var, inv);
   B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize (no alloc)"));
   if (total == 0) return B2_OK;

@@ -70,6 +70,7 @@ _SIGS = {
     "b2_batch_norm_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P],
     "b2_batch_norm_inference": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _F32, _P],
     "b2_batch_norm_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
+    "b2_batch_norm_update_moving": [_P, _P, _P, _P, _P, _I64, _F32, _F32],
     "b2_dense": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_backprop_input": [_P, _P, _P, _P, _P, _P],
     "b2_dense_backprop_weight": [_P, _P, _P, _P, _P, _P],
@@ -315,6 +316,19 @@ def _k_batch_norm_training(x, gamma, beta, epsilon=1e-3):
         _check(_lib.b2_batch_norm_training(_stream(x), _p(x), _I64x4(*x.shape), _p(g), g.numel(), _p(b), b.numel(),
                                            float(epsilon), _p(y), _p(mean), _p(var)))
     return y, mean, var
+
+
+def batch_norm_update_moving(moving_mean, moving_var, batch_mean, batch_var, momentum):
+    """moving = momentum * moving + (1 - momentum) * batch, in place, for the
+    mean and variance buffers in one launch (opencl_tf/layers.py:189-194)."""
+    bufs = (moving_mean, moving_var, batch_mean, batch_var)
+    C = moving_mean.numel()
+    if any(not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous() and t.numel() == C) for t in bufs):
+        raise errors.InvalidArgumentError("moving/batch statistics must be contiguous fp32 CUDA vectors of one length")
+    with _on_device(moving_mean):
+        _check(_lib.b2_batch_norm_update_moving(_stream(moving_mean), _p(moving_mean), _p(moving_var),
+                                                _p(batch_mean), _p(batch_var), C, float(momentum),
+                                                float(1.0 - momentum)))
 
 
 def _k_batch_norm_inference(x, gamma, beta, mean, var, epsilon=1e-3):

@@ -17,6 +17,7 @@ import torch
 from torch import nn
 
 from . import initializers
+from . import _library
 from ._library import raw_ops
 from .ops.conv2d import conv2d
 from .ops.dense import dense
@@ -158,8 +159,8 @@ class OpenCLBatchNormalization(_Layer):
             y, batch_mean, batch_var = raw_ops.opencl_batch_norm_training(x, self.gamma, self.beta,
                                                                           epsilon=self.epsilon)
             with torch.no_grad():
-                self.moving_mean.mul_(self.momentum).add_(batch_mean, alpha=1.0 - self.momentum)
-                self.moving_var.mul_(self.momentum).add_(batch_var, alpha=1.0 - self.momentum)
+                _library.batch_norm_update_moving(self.moving_mean, self.moving_var, batch_mean.detach(),
+                                                  batch_var.detach(), self.momentum)
             return y
         return raw_ops.opencl_batch_norm_inference(x, self.gamma, self.beta, self.moving_mean, self.moving_var,
                                                    epsilon=self.epsilon)

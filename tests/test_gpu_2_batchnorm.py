@@ -105,3 +105,20 @@ def test_bn_bad_shapes(otf):
     with pytest.raises(otf.errors.InvalidArgumentError, match="matching NHWC shapes"):
         otf.batch_norm_grad(torch.zeros(1, 2, 2, 4, device="cuda"), x, torch.ones(3, device="cuda"),
                             torch.zeros(3, device="cuda"), torch.ones(3, device="cuda"))
+
+
+def test_moving_statistics_update_rounding(otf):
+    """The layer's moving-average update (reference opencl_tf/layers.py:189-194,
+    three fp32 tensor ops) runs as one launch with the same rounding."""
+    from opencl_tf import _library as L
+    rng = np.random.default_rng(5)
+    C = 37
+    mm, mv, bm, bv = (rng.standard_normal(C).astype(np.float32) for _ in range(4))
+    t = [torch.from_numpy(a.copy()).cuda() for a in (mm, mv, bm, bv)]
+    L.batch_norm_update_moving(*t, 0.99)
+    m32, om32 = np.float32(0.99), np.float32(1.0 - 0.99)
+    want_m = (m32 * mm).astype(np.float32) + (om32 * bm).astype(np.float32)
+    want_v = (m32 * mv).astype(np.float32) + (om32 * bv).astype(np.float32)
+    assert np.array_equal(t[0].cpu().numpy(), want_m)
+    assert np.array_equal(t[1].cpu().numpy(), want_v)
+    assert np.array_equal(t[2].cpu().numpy(), bm) and np.array_equal(t[3].cpu().numpy(), bv)
