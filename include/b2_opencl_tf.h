@@ -211,6 +211,29 @@ int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* x,
                                     float epsilon, float* y, float* saved_mean,
                                     float* saved_var);
 
+/* OpenclBatchNormTraining followed by OpenclRelu on its output, in one call:
+ * z = relu(BN(x)) with the statistics of b2_batch_norm_training; z is bit-for-
+ * bit the two ops in sequence (src/ops/batchnorm_ops.cc:87-180 then
+ * src/ops/relu_ops.cc), with one pass over x and no intermediate tensor.  Not
+ * an op of the reference: the fusion of the pair its layers run back to back. */
+int b2_batch_norm_relu_training(b2_stream_t stream, const float* x,
+                                const int64_t x_shape[4], const float* gamma,
+                                int64_t gamma_len, const float* beta,
+                                int64_t beta_len, float epsilon, float* z,
+                                float* saved_mean, float* saved_var);
+
+/* The gradient of b2_batch_norm_relu_training: OpenclReluGrad followed by
+ * OpenclBatchNormGrad (src/ops/relu_ops.cc, src/ops/batchnorm_ops.cc:313-416)
+ * given grad_z; the ReLU mask (BN(x) > 0) is recomputed from x, the saved
+ * statistics, gamma and beta exactly as the forward computed it, so the
+ * results equal the two ops in sequence bit for bit. */
+int b2_batch_norm_relu_grad(b2_stream_t stream, const float* grad_z,
+                            const int64_t grad_z_shape[4], const float* x,
+                            const int64_t x_shape[4], const float* gamma,
+                            const float* beta, const float* saved_mean,
+                            const float* saved_var, float epsilon,
+                            float* grad_x, float* grad_gamma, float* grad_beta);
+
 /* The Keras layer's moving-statistics update after a training step,
  * opencl_tf/layers.py:189-194: for c < channels,
  *   moving_mean[c] = momentum * moving_mean[c] + one_minus_momentum * batch_mean[c]

@@ -75,18 +75,29 @@ struct VecT<4> {
   __device__ static void from(const float* o, T* p) { *p = make_float4(o[0], o[1], o[2], o[3]); }
 };
 
+// y of the forward normalisation (batchnorm_kernels.cl:77-80), operation for
+// operation, so a ReLU mask recomputed from it matches the forward's.
+__device__ __forceinline__ float bn_y(float x, float m, float iv, float g, float b) {
+  return __fadd_rn(__fmul_rn(g, __fmul_rn(__fsub_rn(x, m), iv)), b);
+}
+
 // Stage 1.  MODE 0: (sum x, sum x^2).  MODE 1: (sum dy, sum dy * x_hat) with
 // x_hat = (x - mean) * inv_std, inv_std = 1/sqrt(var + eps) per channel.
+// MODE 2: as MODE 1 with dy = (y > 0 ? dz : 0), the gradient through a ReLU
+// applied to the BN output y (the reference's relu_grad), y recomputed from x.
 template <int VEC, int MODE>
 __global__ void __launch_bounds__(kThreads)
     bn_partial_kernel(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ mean,
                       const float* __restrict__ var, float eps, int64_t rows, int C, ChunkGeom geo,
-                      float2* __restrict__ partial) {
+                      float2* __restrict__ partial, const float* __restrict__ gamma = nullptr,
+                      const float* __restrict__ beta = nullptr) {
   using V = typename VecT<VEC>::T;
   __shared__ float s_a[kThreads * VEC];
   __shared__ float s_b[kThreads * VEC];
   __shared__ float s_mean[kThreads * VEC];
   __shared__ float s_inv[kThreads * VEC];
+  __shared__ float s_gam[MODE == 2 ? kThreads * VEC : 1];
+  __shared__ float s_bet[MODE == 2 ? kThreads * VEC : 1];
 
   const int chunk = blockIdx.y;
   const int t = threadIdx.x;
@@ -96,12 +107,16 @@ __global__ void __launch_bounds__(kThreads)
   const bool active = r_off < geo.rpi && group < geo.groups;
   const int c0 = group * VEC;
 
-  if (MODE == 1) {
+  if (MODE >= 1) {
     for (int i = t; i < geo.cg * VEC; i += kThreads) {
       const int c = chunk * geo.cg * VEC + i;
       if (c < C) {
         s_mean[i] = mean[c];
         s_inv[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var[c], eps)));
+        if (MODE == 2) {
+          s_gam[i] = gamma[c];
+          s_bet[i] = beta[c];
+        }
       }
     }
     __syncthreads();
@@ -118,11 +133,13 @@ __global__ void __launch_bounds__(kThreads)
 
   if (active) {
     const int loc = cg_local * VEC;
-    float m[VEC], inv[VEC];
+    float m[VEC], inv[VEC], gm[VEC], bt[VEC];
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
-      m[j] = MODE == 1 ? s_mean[loc + j] : 0.0f;
-      inv[j] = MODE == 1 ? s_inv[loc + j] : 0.0f;
+      m[j] = MODE >= 1 ? s_mean[loc + j] : 0.0f;
+      inv[j] = MODE >= 1 ? s_inv[loc + j] : 0.0f;
+      gm[j] = MODE == 2 ? s_gam[loc + j] : 0.0f;
+      bt[j] = MODE == 2 ? s_bet[loc + j] : 0.0f;
     }
     constexpr int U = 4;  // rows per thread per iteration: U (or 2U) independent loads in flight
     const int64_t step = (int64_t)geo.rpi;
@@ -132,7 +149,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         VecT<VEC>::to(*reinterpret_cast<const V*>(x + (r + u * step) * C + c0), v[u]);
-        if (MODE == 1) VecT<VEC>::to(*reinterpret_cast<const V*>(dy + (r + u * step) * C + c0), g[u]);
+        if (MODE >= 1) VecT<VEC>::to(*reinterpret_cast<const V*>(dy + (r + u * step) * C + c0), g[u]);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -143,8 +160,9 @@ __global__ void __launch_bounds__(kThreads)
             acc_b[j] = fmaf(v[u][j], v[u][j], acc_b[j]);
           } else {
             const float xh = (v[u][j] - m[j]) * inv[j];
-            acc_a[j] += g[u][j];
-            acc_b[j] = fmaf(g[u][j], xh, acc_b[j]);
+            const float gv = MODE == 2 && !(bn_y(v[u][j], m[j], inv[j], gm[j], bt[j]) > 0.0f) ? 0.0f : g[u][j];
+            acc_a[j] += gv;
+            acc_b[j] = fmaf(gv, xh, acc_b[j]);
           }
         }
       }
@@ -164,8 +182,9 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
           const float xh = (v[j] - m[j]) * inv[j];
-          acc_a[j] += g[j];
-          acc_b[j] = fmaf(g[j], xh, acc_b[j]);
+          const float gv = MODE == 2 && !(bn_y(v[j], m[j], inv[j], gm[j], bt[j]) > 0.0f) ? 0.0f : g[j];
+          acc_a[j] += gv;
+          acc_b[j] = fmaf(gv, xh, acc_b[j]);
         }
       }
     }
@@ -281,8 +300,9 @@ __device__ __forceinline__ RowTile row_tile(int64_t rows, const ChunkGeom& geo) 
   return rt;
 }
 
-// y = gamma * ((x - mean) * inv_std) + beta (batchnorm_kernels.cl:77-80).
-template <int VEC>
+// y = gamma * ((x - mean) * inv_std) + beta (batchnorm_kernels.cl:77-80);
+// RELU: the reference's relu applied to y in the same pass (y > 0 ? y : 0).
+template <int VEC, bool RELU>
 __global__ void __launch_bounds__(kThreads)
     bn_normalize_kernel(const float* __restrict__ x, const float* __restrict__ mean,
                         const float* __restrict__ inv_std, const float* __restrict__ gamma,
@@ -300,7 +320,10 @@ __global__ void __launch_bounds__(kThreads)
   }
   auto one = [&](const float* v, float* o) {
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) o[j] = __fadd_rn(__fmul_rn(g[j], __fmul_rn(__fsub_rn(v[j], m[j]), iv[j])), b[j]);
+    for (int j = 0; j < VEC; ++j) {
+      const float yv = bn_y(v[j], m[j], iv[j], g[j], b[j]);
+      o[j] = RELU ? (yv > 0.0f ? yv : 0.0f) : yv;
+    }
   };
   constexpr int U = 4;
   for (; rt.r + (U - 1) * rt.step < rt.r_end; rt.r += U * rt.step) {
@@ -339,17 +362,19 @@ __global__ void __launch_bounds__(kFinThreads) bn_grad_finalize_kernel(
   }
 }
 
-// dx = k1 * (NHW*dy - grad_beta - x_hat*grad_gamma) (batchnorm_kernels.cl:135-142)
-template <int VEC>
+// dx = k1 * (NHW*dy - grad_beta - x_hat*grad_gamma) (batchnorm_kernels.cl:135-142);
+// RELU: dy = (y > 0 ? dz : 0) through a ReLU on the BN output, y recomputed.
+template <int VEC, bool RELU>
 __global__ void __launch_bounds__(kThreads)
     bn_grad_dx_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
                       const float* __restrict__ inv_std, const float* __restrict__ k1,
                       const float* __restrict__ grad_beta, const float* __restrict__ grad_gamma,
-                      float* __restrict__ dx, int64_t rows, int C, float nhw_f, ChunkGeom geo) {
+                      float* __restrict__ dx, int64_t rows, int C, float nhw_f, ChunkGeom geo,
+                      const float* __restrict__ gamma = nullptr, const float* __restrict__ beta = nullptr) {
   using V = typename VecT<VEC>::T;
   RowTile rt = row_tile(rows, geo);
   if (!rt.active) return;
-  float m[VEC], iv[VEC], kk[VEC], db[VEC], dg[VEC];
+  float m[VEC], iv[VEC], kk[VEC], db[VEC], dg[VEC], gm[VEC], bt[VEC];
 #pragma unroll
   for (int j = 0; j < VEC; ++j) {
     m[j] = mean[rt.c0 + j];
@@ -357,12 +382,15 @@ __global__ void __launch_bounds__(kThreads)
     kk[j] = k1[rt.c0 + j];
     db[j] = grad_beta[rt.c0 + j];
     dg[j] = grad_gamma[rt.c0 + j];
+    gm[j] = RELU ? gamma[rt.c0 + j] : 0.0f;
+    bt[j] = RELU ? beta[rt.c0 + j] : 0.0f;
   }
-  auto one = [&](const float* vx, const float* vg, float* o) {
+  auto one = [&](const float* vx, const float* vgz, float* o) {
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       const float xh = __fmul_rn(__fsub_rn(vx[j], m[j]), iv[j]);
-      float t = __fmul_rn(nhw_f, vg[j]);
+      const float gv = RELU && !(__fadd_rn(__fmul_rn(gm[j], xh), bt[j]) > 0.0f) ? 0.0f : vgz[j];
+      float t = __fmul_rn(nhw_f, gv);
       t = __fsub_rn(t, db[j]);
       t = __fsub_rn(t, __fmul_rn(xh, dg[j]));
       o[j] = __fmul_rn(kk[j], t);
@@ -410,39 +438,126 @@ int validate_nhwc(const int64_t* s, const char* what) {
   return B2_OK;
 }
 
+// mode 0: statistics, 1: gradient, 2: gradient through a ReLU on the output
+// (gamma, beta used to recompute the mask).
+template <int VEC>
+void partials_vec(dim3 grid, cudaStream_t s, int mode, const float* x, const float* dy, const float* mean,
+                  const float* var, float eps, int64_t rows, int C, const ChunkGeom& geo, float2* partial,
+                  const float* gamma, const float* beta) {
+  if (mode == 0)
+    bn_partial_kernel<VEC, 0><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+  else if (mode == 1)
+    bn_partial_kernel<VEC, 1><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
+  else
+    bn_partial_kernel<VEC, 2><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial, gamma, beta);
+}
+
 int launch_partials(cudaStream_t s, int mode, const float* x, const float* dy, const float* mean,
                     const float* var, float eps, int64_t rows, int C, bool vec_ok, const DeviceInfo* d,
-                    float2* partial, int* blocks_out) {
+                    float2* partial, int* blocks_out, const float* gamma = nullptr, const float* beta = nullptr) {
   const ChunkGeom geo = chunk_geom(C, vec_ok);
   const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
   dim3 grid(blocks, geo.chunks);
-  if (geo.vec == 4) {
-    if (mode == 0)
-      bn_partial_kernel<4, 0><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
-    else
-      bn_partial_kernel<4, 1><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
-  } else {
-    if (mode == 0)
-      bn_partial_kernel<1, 0><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
-    else
-      bn_partial_kernel<1, 1><<<grid, kThreads, 0, s>>>(x, dy, mean, var, eps, rows, C, geo, partial);
-  }
+  if (geo.vec == 4) partials_vec<4>(grid, s, mode, x, dy, mean, var, eps, rows, C, geo, partial, gamma, beta);
+  else partials_vec<1>(grid, s, mode, x, dy, mean, var, eps, rows, C, geo, partial, gamma, beta);
   *blocks_out = blocks;
   return check_launch(s, mode == 0 ? "bn_reduce_stats" : "bn_backward_reduce");
 }
 
 int launch_normalize(cudaStream_t s, const float* x, const float* mean, const float* inv, const float* gamma,
-                     const float* beta, float* y, int64_t total, int C, bool vec_ok) {
+                     const float* beta, float* y, int64_t total, int C, bool vec_ok, bool relu = false) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   const ChunkGeom geo = chunk_geom(C, vec_ok);
   const int64_t rows = total / C;
   dim3 grid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
-  if (vec_ok)
-    bn_normalize_kernel<4><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
-  else
-    bn_normalize_kernel<1><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+  if (vec_ok) {
+    if (relu) bn_normalize_kernel<4, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+    else bn_normalize_kernel<4, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+  } else {
+    if (relu) bn_normalize_kernel<1, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+    else bn_normalize_kernel<1, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+  }
   return check_launch(s, "bn_normalize");
+}
+
+// Training forward: statistics, then y = BN(x) (relu: y = relu(BN(x))).
+int bn_training(cudaStream_t s, const float* x, const int64_t* x_shape, const float* gamma, int64_t gamma_len,
+                const float* beta, int64_t beta_len, float epsilon, float* y, float* saved_mean, float* saved_var,
+                bool relu) {
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  const int64_t C = x_shape[3];
+  B2_REQUIRE(gamma_len == C && beta_len == C, "gamma/beta size must equal channels");
+  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
+  const int64_t total = rows * C;
+  if (C == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  Scratch part, inv;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
+  B2_RETURN_IF_ERROR(inv.alloc(sizeof(float) * C, s));
+  int used_blocks = 0;
+  B2_RETURN_IF_ERROR(launch_partials(s, 0, x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, vec_ok, d,
+                                     part.as<float2>(), &used_blocks));
+  bn_stats_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+                                                                epsilon, saved_mean, saved_var, inv.as<float>());
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
+  if (total == 0) return B2_OK;
+  return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok, relu);
+}
+
+// Backward: dx, dgamma, dbeta from dy (relu: dy = (y > 0 ? dz : 0) with y
+// recomputed from x, the statistics, gamma and beta).
+int bn_grad(cudaStream_t s, const float* grad_y, const int64_t* grad_y_shape, const float* x,
+            const int64_t* x_shape, const float* gamma, const float* beta, const float* saved_mean,
+            const float* saved_var, float epsilon, float* grad_x, float* grad_gamma, float* grad_beta, bool relu) {
+  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
+  bool same_shape = grad_y_shape != nullptr;
+  for (int i = 0; same_shape && i < 4; ++i) same_shape = grad_y_shape[i] == x_shape[i];
+  B2_REQUIRE(same_shape, "grad_y and x must have matching NHWC shapes");
+  const int64_t C = x_shape[3];
+  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
+  const int64_t total = rows * C;
+  if (C == 0) return B2_OK;
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(grad_y) && aligned16(grad_x);
+  const ChunkGeom geo = chunk_geom(C, vec_ok);
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  Scratch part, chan;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
+  B2_RETURN_IF_ERROR(chan.alloc(sizeof(float) * 2 * C, s));
+  float* k1 = chan.as<float>();
+  float* inv = k1 + C;
+  int used_blocks = 0;
+  B2_RETURN_IF_ERROR(launch_partials(s, relu ? 2 : 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C,
+                                     vec_ok, d, part.as<float2>(), &used_blocks, gamma, beta));
+  bn_grad_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+                                                               epsilon, gamma, saved_var, grad_beta, grad_gamma, k1,
+                                                               inv);
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
+  if (total == 0) return B2_OK;
+  const float nhw_f = (float)(int)rows;
+  dim3 egrid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
+  if (vec_ok) {
+    if (relu)
+      bn_grad_dx_kernel<4, true><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
+                                                           grad_x, rows, (int)C, nhw_f, geo, gamma, beta);
+    else
+      bn_grad_dx_kernel<4, false><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
+                                                            grad_x, rows, (int)C, nhw_f, geo);
+  } else {
+    if (relu)
+      bn_grad_dx_kernel<1, true><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
+                                                           grad_x, rows, (int)C, nhw_f, geo, gamma, beta);
+    else
+      bn_grad_dx_kernel<1, false><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
+                                                            grad_x, rows, (int)C, nhw_f, geo);
+  }
+  return check_launch(s, "bn_backward_dx");
 }
 
 }  // namespace
@@ -457,30 +572,18 @@ int b2_batch_norm_training(b2_stream_t stream, const float* x, const int64_t x_s
                            int64_t gamma_len, const float* beta, int64_t beta_len, float epsilon, float* y,
                            float* saved_mean, float* saved_var) {
   clear_error();
-  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
-  const int64_t C = x_shape[3];
-  B2_REQUIRE(gamma_len == C && beta_len == C, "gamma/beta size must equal channels");
-  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
-  const int64_t total = rows * C;
-  if (C == 0) return B2_OK;
-  const DeviceInfo* d = nullptr;
-  B2_RETURN_IF_ERROR(device_info(&d));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
-  const ChunkGeom geo = chunk_geom(C, vec_ok);
-  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
-  Scratch part, inv;
-  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
-  B2_RETURN_IF_ERROR(inv.alloc(sizeof(float) * C, s));
-  int used_blocks = 0;
-  B2_RETURN_IF_ERROR(launch_partials(s, 0, x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, vec_ok, d,
-                                     part.as<float2>(), &used_blocks));
-  bn_stats_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
-                                                                       epsilon, saved_mean, saved_var,
-                                                                       inv.as<float>());
-  B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
-  if (total == 0) return B2_OK;
-  return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok);
+  return bn_training(static_cast<cudaStream_t>(stream), x, x_shape, gamma, gamma_len, beta, beta_len, epsilon, y,
+                     saved_mean, saved_var, false);
+}
+
+// OpenclBatchNormTraining followed by OpenclRelu (src/ops/batchnorm_ops.cc:87-180,
+// src/ops/relu_ops.cc), one pass over x less and no intermediate tensor.
+int b2_batch_norm_relu_training(b2_stream_t stream, const float* x, const int64_t x_shape[4], const float* gamma,
+                                int64_t gamma_len, const float* beta, int64_t beta_len, float epsilon, float* z,
+                                float* saved_mean, float* saved_var) {
+  clear_error();
+  return bn_training(static_cast<cudaStream_t>(stream), x, x_shape, gamma, gamma_len, beta, beta_len, epsilon, z,
+                     saved_mean, saved_var, true);
 }
 
 // src/ops/batchnorm_ops.cc:213-275
@@ -510,43 +613,21 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y, const int64_t gr
                        const int64_t x_shape[4], const float* gamma, const float* saved_mean,
                        const float* saved_var, float epsilon, float* grad_x, float* grad_gamma, float* grad_beta) {
   clear_error();
-  B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
-  bool same_shape = grad_y_shape != nullptr;
-  for (int i = 0; same_shape && i < 4; ++i) same_shape = grad_y_shape[i] == x_shape[i];
-  B2_REQUIRE(same_shape, "grad_y and x must have matching NHWC shapes");
-  const int64_t C = x_shape[3];
-  const int64_t rows = x_shape[0] * x_shape[1] * x_shape[2];
-  const int64_t total = rows * C;
-  if (C == 0) return B2_OK;
-  const DeviceInfo* d = nullptr;
-  B2_RETURN_IF_ERROR(device_info(&d));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(grad_y) && aligned16(grad_x);
-  const ChunkGeom geo = chunk_geom(C, vec_ok);
-  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
-  Scratch part, chan;
-  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
-  B2_RETURN_IF_ERROR(chan.alloc(sizeof(float) * 2 * C, s));
-  float* k1 = chan.as<float>();
-  float* inv = k1 + C;
-  int used_blocks = 0;
-  B2_RETURN_IF_ERROR(launch_partials(s, 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C, vec_ok, d,
-                                     part.as<float2>(), &used_blocks));
-  bn_grad_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
-                                                                      epsilon, gamma, saved_var, grad_beta,
-                                                                      grad_gamma, k1, inv);
-  B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
-  if (total == 0) return B2_OK;
-  const float nhw_f = (float)(int)rows;
-  dim3 egrid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
-  if (vec_ok) {
-    bn_grad_dx_kernel<4><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x,
-                                                   rows, (int)C, nhw_f, geo);
-  } else {
-    bn_grad_dx_kernel<1><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma, grad_x,
-                                                   rows, (int)C, nhw_f, geo);
-  }
-  return check_launch(s, "bn_backward_dx");
+  return bn_grad(static_cast<cudaStream_t>(stream), grad_y, grad_y_shape, x, x_shape, gamma, nullptr, saved_mean,
+                 saved_var, epsilon, grad_x, grad_gamma, grad_beta, false);
+}
+
+// OpenclReluGrad followed by OpenclBatchNormGrad (src/ops/relu_ops.cc,
+// src/ops/batchnorm_ops.cc:313-416) for z = relu(BN(x)): the ReLU mask is
+// recomputed from x, so neither y nor dy is stored.
+int b2_batch_norm_relu_grad(b2_stream_t stream, const float* grad_z, const int64_t grad_z_shape[4], const float* x,
+                            const int64_t x_shape[4], const float* gamma, const float* beta, const float* saved_mean,
+                            const float* saved_var, float epsilon, float* grad_x, float* grad_gamma,
+                            float* grad_beta) {
+  clear_error();
+  B2_REQUIRE(beta != nullptr && gamma != nullptr, "gamma and beta are required");
+  return bn_grad(static_cast<cudaStream_t>(stream), grad_z, grad_z_shape, x, x_shape, gamma, beta, saved_mean,
+                 saved_var, epsilon, grad_x, grad_gamma, grad_beta, true);
 }
 
 // opencl_tf/layers.py:189-194 (the Keras layer's moving statistics):

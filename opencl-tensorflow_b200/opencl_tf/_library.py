@@ -71,6 +71,8 @@ _SIGS = {
     "b2_batch_norm_inference": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _F32, _P],
     "b2_batch_norm_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
     "b2_batch_norm_update_moving": [_P, _P, _P, _P, _P, _I64, _F32, _F32],
+    "b2_batch_norm_relu_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P],
+    "b2_batch_norm_relu_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
     "b2_dense": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_backprop_input": [_P, _P, _P, _P, _P, _P],
     "b2_dense_backprop_weight": [_P, _P, _P, _P, _P, _P],
@@ -331,6 +333,40 @@ def batch_norm_update_moving(moving_mean, moving_var, batch_mean, batch_var, mom
                                                 float(1.0 - momentum)))
 
 
+def _k_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3):
+    x = _input(x, "x")
+    g = _input(gamma, "gamma")
+    b = _input(beta, "beta")
+    _rank(x, 4, "x must be NHWC")
+    C = x.shape[3]
+    z = torch.empty_like(x)
+    mean = torch.empty(C, device=x.device, dtype=torch.float32)
+    var = torch.empty(C, device=x.device, dtype=torch.float32)
+    with _on_device(x):
+        _check(_lib.b2_batch_norm_relu_training(_stream(x), _p(x), _I64x4(*x.shape), _p(g), g.numel(), _p(b),
+                                                b.numel(), float(epsilon), _p(z), _p(mean), _p(var)))
+    return z, mean, var
+
+
+def _k_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, epsilon=1e-3):
+    dz = _input(grad_z, "grad_z")
+    x = _input(x, "x")
+    g, b = _input(gamma, "gamma"), _input(beta, "beta")
+    m, v = _input(saved_mean, "saved_mean"), _input(saved_var, "saved_var")
+    if x.dim() != 4 or dz.shape != x.shape:
+        raise errors.InvalidArgumentError("grad_z and x must have matching NHWC shapes")
+    C = x.shape[3]
+    if g.numel() < C or b.numel() < C or m.numel() < C or v.numel() < C:
+        raise errors.InvalidArgumentError("gamma/beta/saved_mean/saved_var must have C elements")
+    dx = torch.empty_like(x)
+    dg = torch.empty(C, device=x.device, dtype=torch.float32)
+    db = torch.empty(C, device=x.device, dtype=torch.float32)
+    with _on_device(x):
+        _check(_lib.b2_batch_norm_relu_grad(_stream(x), _p(dz), _I64x4(*dz.shape), _p(x), _I64x4(*x.shape), _p(g),
+                                            _p(b), _p(m), _p(v), float(epsilon), _p(dx), _p(dg), _p(db)))
+    return dx, dg, db
+
+
 def _k_batch_norm_inference(x, gamma, beta, mean, var, epsilon=1e-3):
     x = _input(x, "x")
     g, b = _input(gamma, "gamma"), _input(beta, "beta")
@@ -557,6 +593,7 @@ def _mk_raw_ops():
     def opencl_batch_norm_grad(grad_y, x, gamma, saved_mean, saved_var, epsilon=1e-3):
         return _k_batch_norm_grad(grad_y, x, gamma, saved_mean, saved_var, float(epsilon))
 
+
     def opencl_dense(x, w, b):
         return _apply("OpenclDense", _k_dense, (x, w, b), {})
 
@@ -583,6 +620,26 @@ def _mk_raw_ops():
 
 raw_ops = _mk_raw_ops()
 """One function per reference op, named as TF names the op library's ops."""
+
+
+def _mk_fused_ops():
+    ns = types.SimpleNamespace()
+
+    def opencl_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3):
+        return _apply("OpenclBatchNormReluTraining", _k_batch_norm_relu_training, (x, gamma, beta),
+                      {"epsilon": float(epsilon)}, nondiff=(1, 2))
+
+    def opencl_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, epsilon=1e-3):
+        return _k_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, float(epsilon))
+
+    ns.opencl_batch_norm_relu_training = opencl_batch_norm_relu_training
+    ns.opencl_batch_norm_relu_grad = opencl_batch_norm_relu_grad
+    return ns
+
+
+fused_ops = _mk_fused_ops()
+"""Ops with no counterpart in the reference: pairs its layers run back to back
+(BatchNormTraining -> Relu), fused, with bit-identical results."""
 
 
 # ------------------------------------------------------- runtime utilities

@@ -20,7 +20,7 @@ never computes a gradient for the image batch.
 """
 from __future__ import annotations
 
-from ._library import RegisterGradient, raw_ops
+from ._library import RegisterGradient, fused_ops, raw_ops
 
 
 def _host_shape(t):
@@ -62,6 +62,15 @@ def _batch_norm_training_grad(op, grad_y, grad_mean=None, grad_var=None):
     _y, saved_mean, saved_var = op.outputs
     gx, ggamma, gbeta = raw_ops.opencl_batch_norm_grad(grad_y, x, gamma, saved_mean, saved_var,
                                                        epsilon=op.get_attr("epsilon"))
+    return [gx, ggamma, gbeta]
+
+
+@RegisterGradient("OpenclBatchNormReluTraining")
+def _batch_norm_relu_training_grad(op, grad_z, grad_mean=None, grad_var=None):
+    x, gamma, beta = op.inputs
+    _z, saved_mean, saved_var = op.outputs
+    gx, ggamma, gbeta = fused_ops.opencl_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var,
+                                                            epsilon=op.get_attr("epsilon"))
     return [gx, ggamma, gbeta]
 
 

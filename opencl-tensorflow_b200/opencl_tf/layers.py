@@ -165,6 +165,21 @@ class OpenCLBatchNormalization(_Layer):
         return raw_ops.opencl_batch_norm_inference(x, self.gamma, self.beta, self.moving_mean, self.moving_var,
                                                    epsilon=self.epsilon)
 
+    def forward_relu(self, x, training=None):
+        """relu(self(x)): this layer followed by an OpenCLReLU, the pair the
+        reference's networks chain, as one fused op when training (bit-identical
+        values and gradients, one pass over x and no intermediate tensor)."""
+        if training is None:
+            training = self.training
+        if bool(training):
+            z, batch_mean, batch_var = _library.fused_ops.opencl_batch_norm_relu_training(x, self.gamma, self.beta,
+                                                                               epsilon=self.epsilon)
+            with torch.no_grad():
+                _library.batch_norm_update_moving(self.moving_mean, self.moving_var, batch_mean.detach(),
+                                                  batch_var.detach(), self.momentum)
+            return z
+        return relu(self.forward(x, training=False))
+
     def get_config(self):
         cfg = super().get_config()
         cfg.update(momentum=self.momentum, epsilon=self.epsilon)

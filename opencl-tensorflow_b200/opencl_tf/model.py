@@ -6,6 +6,10 @@ built from this package's layers:
     dsconv_block(144, strides=2)
     Flatten -> Dense(128) -> ReLU -> Reshape(4, 4, 8) -> UpSampling2D(2x) -> Sigmoid
 
+Each BatchNormalization -> ReLU pair runs as one fused op in training
+(``fuse_bn_relu=True``, the default): the same values and gradients bit for
+bit as the two layers in sequence, one activation pass fewer each way.
+
 ``build_model(widened=True)`` gives the larger variant used for scaling runs:
 input 256x256x3, filters 96/192/288, Dense 512, Reshape(8, 8, 8) -> 16x16x8.
 All activations are NHWC float32 on the GPU; Flatten/Reshape are free views.
@@ -27,8 +31,10 @@ def _same_out(n: int, s: int) -> int:
 
 class BuildModel(nn.Module):
     def __init__(self, input_shape: Sequence[int] = (64, 64, 3), filters: Sequence[int] = (48, 96, 144),
-                 dense_units: int = 128, head: Sequence[int] = (4, 4, 8), upsample=(2, 2), device=None):
+                 dense_units: int = 128, head: Sequence[int] = (4, 4, 8), upsample=(2, 2), device=None,
+                 fuse_bn_relu: bool = True):
         super().__init__()
+        self.fuse_bn_relu = bool(fuse_bn_relu)
         H, W, C = (int(v) for v in input_shape)
         self.input_shape = (H, W, C)
         self.head = tuple(int(v) for v in head)
@@ -63,19 +69,24 @@ class BuildModel(nn.Module):
         self.sigmoid = OpenCLSigmoid()
         self.output_shape = (self.head[0] * self.up.size[0], self.head[1] * self.up.size[1], self.head[2])
 
+    def _bn_relu(self, bn, relu, x, training):
+        if self.fuse_bn_relu:
+            return bn.forward_relu(x, training=training)
+        return relu(bn(x, training=training))
+
     def forward(self, x, training=None):
-        x = self.stem_relu(self.stem_bn(self.stem_conv(x), training=training))
+        x = self._bn_relu(self.stem_bn, self.stem_relu, self.stem_conv(x), training)
         for dw, bn1, r1, pw, bn2, r2 in self.blocks:
-            x = r1(bn1(dw(x), training=training))
-            x = r2(bn2(pw(x), training=training))
+            x = self._bn_relu(bn1, r1, dw(x), training)
+            x = self._bn_relu(bn2, r2, pw(x), training)
         x = x.reshape(x.shape[0], -1)
         x = self.dense_relu(self.dense(x))
         x = x.reshape(x.shape[0], *self.head)
         return self.sigmoid(self.up(x))
 
 
-def build_model(widened: bool = False, device=None) -> BuildModel:
+def build_model(widened: bool = False, device=None, fuse_bn_relu: bool = True) -> BuildModel:
     """The README model; ``widened=True`` for the 256x256 / 96-192-288 / Dense 512 variant."""
     if widened:
-        return BuildModel((256, 256, 3), (96, 192, 288), 512, (8, 8, 8), device=device)
-    return BuildModel(device=device)
+        return BuildModel((256, 256, 3), (96, 192, 288), 512, (8, 8, 8), device=device, fuse_bn_relu=fuse_bn_relu)
+    return BuildModel(device=device, fuse_bn_relu=fuse_bn_relu)

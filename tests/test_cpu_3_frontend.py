@@ -34,8 +34,10 @@ def test_python_api_names():
 
 
 def test_gradient_registry_matches_reference_wiring():
-    assert set(_GRADIENTS) == {"OpenclConv2d", "OpenclDepthwiseConv2d", "OpenclRelu", "OpenclBatchNormTraining",
-                               "OpenclSigmoid", "OpenclDense", "OpenclUpsamplingBilinear2d"}
+    reference = {"OpenclConv2d", "OpenclDepthwiseConv2d", "OpenclRelu", "OpenclBatchNormTraining", "OpenclSigmoid",
+                 "OpenclDense", "OpenclUpsamplingBilinear2d"}
+    # the reference's registrations, plus the fused BatchNorm -> ReLU pair (an extension, not a reference op)
+    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining"}
     assert "OpenclBatchNormInference" not in _GRADIENTS
 
 

@@ -122,3 +122,25 @@ def test_moving_statistics_update_rounding(otf):
     assert np.array_equal(t[0].cpu().numpy(), want_m)
     assert np.array_equal(t[1].cpu().numpy(), want_v)
     assert np.array_equal(t[2].cpu().numpy(), bm) and np.array_equal(t[3].cpu().numpy(), bv)
+
+
+@pytest.mark.parametrize("shape", [(4, 6, 5, 8), (3, 7, 5, 3), (2, 64, 32, 48)])
+def test_fused_bn_relu_equals_the_two_ops(otf, shape):
+    """BatchNormTraining -> Relu fused (forward) and ReluGrad -> BatchNormGrad
+    fused (backward, mask recomputed from x) equal the reference ops in
+    sequence bit for bit."""
+    from opencl_tf import _library as L
+    rng = np.random.default_rng(11)
+    C = shape[-1]
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * 2 + 0.3).cuda()
+    g = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).cuda()
+    dz = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).cuda()
+    y, m, v = L._k_batch_norm_training(x, g, b, 1e-3)
+    z_ref = L._k_relu(y)
+    z, m2, v2 = L._k_batch_norm_relu_training(x, g, b, 1e-3)
+    assert torch.equal(z, z_ref) and torch.equal(m, m2) and torch.equal(v, v2)
+    dy = L._k_relu_grad(dz, y)
+    dx_ref, dg_ref, db_ref = L._k_batch_norm_grad(dy, x, g, m, v, 1e-3)
+    dx, dg, db = L._k_batch_norm_relu_grad(dz, x, g, b, m, v, 1e-3)
+    assert torch.equal(dx, dx_ref) and torch.equal(dg, dg_ref) and torch.equal(db, db_ref)

@@ -149,3 +149,26 @@ def test_keras_like_layers_train(otf, layer_fn):
     for _ in range(5):
         l1 = step()
     assert l1 < l0
+
+
+def test_fused_bn_relu_model_matches_unfused(otf):
+    """The README model with its BatchNorm -> ReLU pairs fused gives the same
+    loss, gradients and moving statistics as with the separate layers."""
+    from opencl_tf.model import build_model
+    from opencl_tf.train import mse
+    torch.manual_seed(0)
+    fused = build_model(device="cuda")
+    plain = build_model(device="cuda", fuse_bn_relu=False)
+    plain.load_state_dict(fused.state_dict())
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.rand(8, 64, 64, 3, device="cuda", generator=g)
+    t = torch.rand(8, 8, 8, 8, device="cuda", generator=g)
+    lf = mse(fused(x, training=True), t)
+    lp = mse(plain(x, training=True), t)
+    lf.backward()
+    lp.backward()
+    assert torch.equal(lf, lp)
+    for (n, a), (_, b) in zip(fused.named_parameters(), plain.named_parameters()):
+        assert torch.equal(a.grad, b.grad), n
+    for (n, a), (_, b) in zip(fused.named_buffers(), plain.named_buffers()):
+        assert torch.equal(a, b), n
