@@ -181,6 +181,19 @@ def cpu_reference_steps(widened, sample_images, steps, warmup, min_seconds=0.0):
     return sample_images * done / dt, o.threads(), kind, dt, done
 
 
+# DRAM bytes (read + write) of one launch of the dominant op's kernel, from
+# one ncu capture of that workload; keyed by op and its algorithmic bytes so a
+# different workload reports null.  Source: the named summary under profiles/.
+NCU_TRAFFIC = {
+    ("conv2d_backprop_filter", 113258304): (117454592, "profiles/tma_gemm_conv_wgrad_readme_stem.md"),
+}
+
+
+def ncu_traffic(op, algorithmic_bytes):
+    """(DRAM bytes per launch, summary file) or (None, None)."""
+    return NCU_TRAFFIC.get((op, int(algorithmic_bytes)), (None, None))
+
+
 # ------------------------------------------------------------------ ours
 
 def run_ours(args, rank, world, local_rank):
@@ -315,7 +328,8 @@ def run_ours(args, rank, world, local_rank):
         top = max(rows, key=lambda r: r["ms"])
         roof = {"kernel": top["op"], "bound": top["bound"], "achieved": round(top["achieved"], 1),
                 "peak": round(top["peak"], 1), "unit": top["unit"], "frac": round(top["frac"], 4),
-                "peak_source": profile.peaks()["source"], "traffic": None,
+                "peak_source": profile.peaks()["source"], "traffic": ncu_traffic(top["op"], top["bytes"])[0],
+                "traffic_source": ncu_traffic(top["op"], top["bytes"])[1],
                 "algorithmic_bytes": top["bytes"], "algorithmic_flops": top["flops"], "ms": round(top["ms"], 4),
                 "step_ms_sum_of_ops": round(sum(r["ms"] for r in rows), 4)}
         model.zero_grad(set_to_none=True)
