@@ -271,6 +271,199 @@ __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_vec4_kernel(const f
   }
 }
 
+// ------------------------------------------ staged filter gradient
+//
+// dm == 1, C % 4 == 0, kH*kW <= 9, 16-byte aligned, staged rows fit: CTA
+// (output-row band, channel chunk) walks output rows r0 .. r1 (r = n*Ho + ho)
+// through a ring of S shared-memory slots.  Thread 0 fills a slot with 1-D bulk
+// copies (cp.async.bulk, completion on the slot's mbarrier): the dy row and the
+// kH input rows the output row reads, each input row placed after padL zero
+// pixels so every tap of every output column lands inside the slot; rows
+// outside the image are flagged and their taps skipped.  Threads (x, y) =
+// (channel group, output-column lane) accumulate all taps of their 4 channels
+// from shared memory; the CTA folds its column lanes per tap in a fixed order
+// (deterministic).  Every wait is bounded.
+
+static __device__ unsigned int g_dw_timeouts = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool bar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of parity `parity`, at most 10 s; a timeout is counted.
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (!bar_try_wait(b, parity)) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 10ull * 1000 * 1000 * 1000) {
+      atomicAdd(&g_dw_timeouts, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void bulk_g2s(float* dst, const float* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+struct DwStage {
+  int slots;       // S
+  int padL;        // zero pixels staged before each input row
+  int Wp;          // staged input row width (pixels)
+  int slot_floats; // Wo*C + kH*Wp*C
+};
+
+constexpr int kStagedConsumers = 256;  // consumer threads of a staged CTA (one producer warp on top)
+
+// Warp 0 produces (lane 0 issues the bulk copies of the next row into a slot
+// once its EMPTY barrier shows every consumer warp is done with it); the other
+// warps consume rows as their FULL barriers complete, without block-wide
+// synchronisation, and arrive on EMPTY per warp.
+template <int KMAX>
+__global__ void __launch_bounds__(32 + kStagedConsumers) dw_wgrad_staged_kernel(const float* __restrict__ x,
+                                                                               const float* __restrict__ dy,
+                                                                               float* __restrict__ partial,
+                                                                               DwArgs a, DwStage st, int cgx,
+                                                                               int lanes_y, int rows_per_block) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  float* slots = reinterpret_cast<float*>(dsm);
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)st.slots * st.slot_floats * 4);
+  uint64_t* empty = full + st.slots;
+  int* valid = reinterpret_cast<int*>(empty + st.slots);  // [S][kH]
+  __shared__ float4 s_fold[kStagedConsumers];
+
+  const int C = a.C, cg = C >> 2;
+  const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int ct = tid - 32;  // consumer index
+  const int cgl = ct % cgx, ly = ct / cgx;
+  const bool consumer = warp > 0 && ly < lanes_y;
+  const bool active = consumer && cgl < cg;
+  const int c = 4 * cgl;
+  const int consumer_warps = (32 * ((cgx * lanes_y + 31) / 32)) / 32;
+  const int taps = a.kH * a.kW;
+  const int rows = a.N * a.Ho;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int nr = (r0 + rows_per_block < rows ? r0 + rows_per_block : rows) - r0;
+  const int dy_floats = a.Wo * C;
+
+  // Zero the slots once (the padding pixels stay zero), make the generic
+  // writes visible to the bulk copies, then set up the barriers.
+  for (int i = tid; i < st.slots * st.slot_floats; i += nthr) slots[i] = 0.0f;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (tid == 0) {
+    for (int i = 0; i < st.slots; ++i) {
+      bar_init(&full[i], 1);
+      bar_init(&empty[i], consumer_warps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  float4 acc[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nr; ++i, ++issued) {
+        const int sl = i % st.slots;
+        if (i >= st.slots && !bar_wait(&empty[sl], (uint32_t)(i / st.slots - 1) & 1u)) break;
+        const int r = r0 + i;
+        const int n = r / a.Ho, ho = r - n * a.Ho;
+        float* base = slots + (size_t)sl * st.slot_floats;
+        uint32_t bytes = (uint32_t)dy_floats * 4u;
+        for (int kh = 0; kh < a.kH; ++kh) {
+          const int hi = ho * a.sH - a.pH + kh;
+          const bool ok = (unsigned)hi < (unsigned)a.H;
+          valid[sl * a.kH + kh] = ok;
+          if (ok) bytes += (uint32_t)(a.W * C) * 4u;
+        }
+        bar_expect_tx(&full[sl], bytes);
+        bulk_g2s(base, dy + (int64_t)r * dy_floats, (uint32_t)dy_floats * 4u, &full[sl]);
+        for (int kh = 0; kh < a.kH; ++kh) {
+          const int hi = ho * a.sH - a.pH + kh;
+          if ((unsigned)hi < (unsigned)a.H)
+            bulk_g2s(base + dy_floats + (kh * st.Wp + st.padL) * C, x + ((int64_t)(n * a.H + hi) * a.W) * C,
+                     (uint32_t)(a.W * C) * 4u, &full[sl]);
+        }
+      }
+      // let every issued copy land before the CTA can exit
+      const int first = issued > st.slots ? issued - st.slots : 0;
+      for (int i = first; i < issued; ++i) bar_wait(&full[i % st.slots], (uint32_t)(i / st.slots) & 1u);
+    }
+  } else if (ct < consumer_warps * 32) {
+    for (int i = 0; i < nr; ++i) {
+      const int sl = i % st.slots;
+      if (!bar_wait(&full[sl], (uint32_t)(i / st.slots) & 1u)) break;
+      const float* base = slots + (size_t)sl * st.slot_floats;
+      if (active) {
+        for (int wo = ly; wo < a.Wo; wo += lanes_y) {
+          const float4 g = *reinterpret_cast<const float4*>(base + wo * C + c);
+          const float* xcol = base + dy_floats + (wo * a.sW) * C + c;
+#pragma unroll
+          for (int k = 0; k < KMAX; ++k) {
+            if (k < taps) {
+              const int kh = k / a.kW, kw = k - kh * a.kW;
+              if (valid[sl * a.kH + kh] != 0) {
+                const float4 xv = *reinterpret_cast<const float4*>(xcol + (kh * st.Wp + kw) * C);
+                acc[k].x = fmaf(xv.x, g.x, acc[k].x);
+                acc[k].y = fmaf(xv.y, g.y, acc[k].y);
+                acc[k].z = fmaf(xv.z, g.z, acc[k].z);
+                acc[k].w = fmaf(xv.w, g.w, acc[k].w);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[sl])) : "memory");
+    }
+  }
+  const int64_t out_base = (int64_t)blockIdx.x * taps * C;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    if (k >= taps) break;
+    __syncthreads();
+    if (consumer) s_fold[ct] = acc[k];
+    __syncthreads();
+    if (consumer && ly == 0 && cgl < cg) {
+      float4 sum = s_fold[cgl];
+      for (int l = 1; l < lanes_y; ++l) sum = fadd4(sum, s_fold[l * cgx + cgl]);
+      *reinterpret_cast<float4*>(partial + out_base + (int64_t)k * C + c) = sum;
+    }
+  }
+}
+
 // Stage 1, any shape: one CTA per (pixel chunk, filter-element chunk); each
 // thread owns one filter element and walks the chunk's pixels.
 __global__ void __launch_bounds__(kThreads) dw_wgrad_partial_scalar_kernel(const float* __restrict__ x,
@@ -348,6 +541,15 @@ int dw_forward_geom(const int64_t* input_shape, const int64_t* filter_shape, con
 }
 
 }  // namespace
+
+// Expired bounded waits of the staged depthwise kernels (read by
+// b2_device_timeouts).
+unsigned int dw_timeouts() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_dw_timeouts, sizeof(v));
+  return v;
+}
+
 }  // namespace b2
 
 using namespace b2;
@@ -454,7 +656,38 @@ int b2_depthwise_conv2d_backprop_filter(b2_stream_t stream, const float* input, 
   const bool vec = g.dm == 1 && g.Ci % 4 == 0 && taps <= 9 && aligned16(input) && aligned16(out_backprop);
   Scratch part;
   int blocks = 0;
-  if (vec) {
+  // staged path: slots of (dy row + kH padded input rows) fit ~100 KB x S
+  const int64_t padL = g.pW;
+  int64_t padR = (g.Wo - 1) * g.sW + g.kW - (g.W + padL);
+  if (padR < 0) padR = 0;
+  const int64_t Wp = g.W + padL + padR;
+  const int64_t slot_floats = g.Wo * g.Ci + g.kH * Wp * g.Ci;
+  const int64_t slots = slot_floats > 0 ? (int64_t)100 * 1024 / (slot_floats * 4) : 0;
+  if (vec && slots >= 2 && g.Ci / 4 <= kStagedConsumers && g.N * g.Ho <= kMaxInt32) {
+    const DwStage st{(int)(slots > 6 ? 6 : slots), (int)padL, (int)Wp, (int)slot_floats};
+    const size_t smem = (size_t)st.slots * st.slot_floats * 4 + 16 * st.slots + 4 * st.slots * g.kH + 16;
+    static bool configured = false;
+    if (!configured) {
+      B2_CUDA_OR_RETURN(cudaFuncSetAttribute(dw_wgrad_staged_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             110 * 1024));
+      configured = true;
+    }
+    const int cgx = (int)(g.Ci / 4);
+    int lanes_y = kStagedConsumers / cgx;
+    if (lanes_y > g.Wo) lanes_y = (int)g.Wo;
+    const int nthreads = 32 + ((cgx * lanes_y + 31) / 32) * 32;
+    const int64_t rows = g.N * g.Ho;
+    int per_sm = 0;
+    B2_CUDA_OR_RETURN(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dw_wgrad_staged_kernel<9>, nthreads,
+                                                                    smem));
+    int64_t want = (int64_t)d->sm_count * (per_sm > 0 ? per_sm : 1);
+    blocks = (int)(want < rows ? want : rows);
+    const int64_t rpb = ceil_div(rows, blocks);
+    blocks = (int)ceil_div(rows, rpb);
+    B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * blocks * F, s));
+    dw_wgrad_staged_kernel<9><<<blocks, nthreads, smem, s>>>(input, out_backprop, part.as<float>(), a, st, cgx,
+                                                              lanes_y, (int)rpb);
+  } else if (vec) {
     const int cg_total = (int)(g.Ci / 4);
     const int cg_per_cta = cg_total < kThreads ? cg_total : kThreads;
     const int chunks = (int)ceil_div(cg_total, cg_per_cta);

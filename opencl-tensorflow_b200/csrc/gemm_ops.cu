@@ -28,6 +28,8 @@
 #include "tma_gemm.cuh"
 
 namespace b2 {
+unsigned int dw_timeouts();  // depthwise.cu
+
 namespace tc {
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N,
@@ -761,6 +763,7 @@ int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_
 int b2_device_timeouts(unsigned int* count) {
   clear_error();
   B2_CUDA_OR_RETURN(cudaMemcpyFromSymbol(count, g_tc_timeouts, sizeof(unsigned int)));
+  *count += b2::dw_timeouts();
   return B2_OK;
 }
 

@@ -71,3 +71,16 @@ def test_dwconv2d_bad_args(otf):
         otf.depthwise_conv2d_backprop_input([1, 5, 5, 4], torch.zeros(3, 3, 4, 1, device="cuda"),
                                             torch.zeros(1, 4, 5, 4, device="cuda"), strides=(1, 1, 1, 1),
                                             padding="SAME")
+
+
+@pytest.mark.parametrize("shape_x,ws,st,padding", [((2, 20, 6, 8), (9, 1, 8, 1), (1, 1, 1, 1), "SAME"),
+                                                   ((3, 12, 10, 16), (1, 9, 16, 1), (1, 2, 1, 1), "SAME"),
+                                                   ((2, 30, 33, 4), (3, 3, 4, 1), (1, 2, 2, 1), "VALID")])
+def test_dwconv2d_filter_grad_tall_and_wide_taps(otf, port, shape_x, ws, st, padding):
+    """Filter gradients with 9 taps in one direction and odd widths (staged-row
+    path: up to nine kernel rows per output row, right padding columns)."""
+    x, w = _inputs(9, shape_x, ws)
+    ry = port.depthwise_conv2d(x, w, st, padding)
+    dy = np.random.default_rng(10).standard_normal(ry.shape).astype(np.float32)
+    dw = otf.depthwise_conv2d_backprop_filter(_cuda(x), list(ws), _cuda(dy), strides=st, padding=padding)
+    assert_close(to_np(dw), port.depthwise_conv2d_backprop_filter(x, ws, dy, st, padding), what="dw")
