@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+from torch.distributed import distributed_c10d as c10d
 
 
 def mse(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
@@ -25,20 +26,84 @@ def mse(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
 
 class GradientAverager:
     """Averages the gradients of ``params`` across the default process group
-    with one bucketed all-reduce (a no-op on a single process)."""
+    (a no-op on a single process).
 
-    def __init__(self, params, group=None):
+    On CUDA (NCCL) the gradients are averaged in place by coalesced all-reduces
+    -- one NCCL group per bucket, no copies through a flat buffer.  With
+    ``overlap`` (the default) the parameters are grouped into buckets of about
+    ``bucket_bytes`` in reverse order (the order backward produces them) and a
+    bucket's all-reduce is launched on a communication stream as soon as its
+    last gradient is accumulated, so the exchange of the Dense layer's large
+    weight gradient runs under the rest of the backward pass; ``begin()``
+    before ``backward()`` arms it and calling the averager afterwards joins the
+    communication stream back.  On CPU (gloo, which has no AVG) the gradients
+    go through one flat buffer, summed and divided.
+    """
+
+    def __init__(self, params, group=None, overlap: bool = True, bucket_bytes: int = 4 << 20):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.flat = None
+        self.armed = False
+        self.overlap = bool(overlap) and self.world > 1 and bool(self.params) and self.params[0].is_cuda
+        if self.overlap:
+            self.buckets, cur, nbytes = [], [], 0
+            for p in reversed(self.params):
+                cur.append(p)
+                nbytes += p.numel() * p.element_size()
+                if nbytes >= bucket_bytes:
+                    self.buckets.append(cur)
+                    cur, nbytes = [], 0
+            if cur:
+                self.buckets.append(cur)
+            self.bucket_of = {p: b for b, ps in enumerate(self.buckets) for p in ps}
+            self.comm = torch.cuda.Stream(device=self.params[0].device)
+            for p in self.params:
+                p.register_post_accumulate_grad_hook(self._grad_ready)
+
+    def begin(self) -> None:
+        """Arm the overlapped reduction for the next backward pass."""
+        if self.overlap:
+            self.ready = [0] * len(self.buckets)
+            self.launched = 0
+            self.armed = True
+
+    def _grad_ready(self, p) -> None:
+        if not self.armed:
+            return
+        b = self.bucket_of[p]
+        self.ready[b] += 1
+        if self.ready[b] == len(self.buckets[b]):
+            self._reduce_bucket(b)
+
+    def _reduce_bucket(self, b) -> None:
+        grads = [q.grad for q in self.buckets[b]]
+        dev = grads[0].device
+        self.comm.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.comm):
+            with c10d._coalescing_manager(self.group, dev):
+                for g in grads:
+                    dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+        self.launched += 1
 
     def __call__(self) -> None:
         if self.world == 1:
             return
+        if self.armed:
+            self.armed = False
+            if self.launched != len(self.buckets):
+                raise RuntimeError("a parameter has no gradient; every rank must produce every gradient")
+            torch.cuda.current_stream(self.params[0].device).wait_stream(self.comm)
+            return
         grads = [p.grad for p in self.params]
         if any(g is None for g in grads):
             raise RuntimeError("a parameter has no gradient; every rank must produce every gradient")
+        if grads[0].is_cuda:
+            with c10d._coalescing_manager(self.group, grads[0].device):
+                for g in grads:
+                    dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+            return
         total = sum(g.numel() for g in grads)
         if self.flat is None or self.flat.numel() != total or self.flat.device != grads[0].device:
             self.flat = torch.empty(total, dtype=grads[0].dtype, device=grads[0].device)
@@ -47,11 +112,8 @@ class GradientAverager:
             n = g.numel()
             self.flat[off:off + n].copy_(g.reshape(-1))
             off += n
-        if self.flat.is_cuda:
-            dist.all_reduce(self.flat, op=dist.ReduceOp.AVG, group=self.group)
-        else:  # gloo has no AVG
-            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
-            self.flat.div_(self.world)
+        dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
+        self.flat.div_(self.world)
         off = 0
         for g in grads:
             n = g.numel()
@@ -78,6 +140,7 @@ class TrainStep:
     def _eager(self, x, y):
         self.opt.zero_grad(set_to_none=True)
         loss = mse(self.model(x, training=True), y)
+        self.avg.begin()
         loss.backward()
         self.avg()
         self.opt.step()

@@ -51,6 +51,17 @@ def _worker(rank, world, port, q):
             dist.all_gather(slot, m)
         err = max(float((p.grad - torch.stack(s).mean(0)).abs().max()) for p, s in zip(model.parameters(), gathered))
         model.zero_grad(set_to_none=True)
+        # 1b) the overlapped path (bucket all-reduces launched from gradient
+        # hooks during backward) gives the same averages
+        avg = GradientAverager(model.parameters())
+        assert avg.overlap and len(avg.buckets) >= 2
+        avg.begin()
+        mse(model(x, training=True), t).backward()
+        avg()
+        torch.cuda.synchronize()
+        err = max(err, max(float((p.grad - torch.stack(s).mean(0)).abs().max())
+                           for p, s in zip(model.parameters(), gathered)))
+        model.zero_grad(set_to_none=True)
         # 2) graphed steps keep the replicas identical
         step = TrainStep(model, graphed=True, warmup=3)
         for _ in range(3):
