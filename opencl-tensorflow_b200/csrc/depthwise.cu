@@ -156,6 +156,74 @@ __global__ void __launch_bounds__(kThreads) dw_dgrad_rows_kernel(const float* __
   }
 }
 
+// depthwise_conv2d_kernels.cl:59-104 for the 3x3, stride-2 case (dm == 1,
+// C % 4 == 0): thread (x, y) of CTA (row band, channel chunk) produces, for
+// each input row of the band, the two input columns with wi + pW = 2j and
+// 2j + 1 for its 4 channels.  Those columns are reached by kw = 0, 2 (dy
+// columns j, j - 1) and kw = 1 (dy column j), so each dy element loaded
+// serves both outputs, and the filter stays in registers.  Taps are added in
+// the reference's (kh, kw) order with round-to-nearest multiply and add.
+__global__ void __launch_bounds__(kThreads) dw_dgrad_s2k3_kernel(const float* __restrict__ dy,
+                                                                  const float* __restrict__ w,
+                                                                  float* __restrict__ dx, DwArgs a, int pairs,
+                                                                  int rows_per_block) {
+  const int c4 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c4 >= (a.C >> 2)) return;
+  const int C = a.C, c = 4 * c4;
+  float4 wr[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) wr[k] = __ldg(reinterpret_cast<const float4*>(w + k * C + c));
+  const int rows = a.N * a.H;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
+  // One input row: taps of rows ho_t (kh ascending), filter rows W0, W1, W2
+  // of those taps; nt = 1 or 2 valid row taps.
+  auto row = [&](const float* gimg, float* xrow, int nt, int ho_a, int ho_b, const float4* wa, const float4* wb) {
+    for (int j = threadIdx.y; j < pairs; j += blockDim.y) {
+      const bool okj = j < a.Wo, okj1 = j >= 1 && j - 1 < a.Wo;
+      const float* ra = gimg + (int64_t)ho_a * a.Wo * C;
+      const float* rb = gimg + (int64_t)(nt > 1 ? ho_b : ho_a) * a.Wo * C;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 ga = nt > 0 && okj ? __ldg(reinterpret_cast<const float4*>(ra + (int64_t)j * C)) : z;
+      const float4 gb = nt > 0 && okj1 ? __ldg(reinterpret_cast<const float4*>(ra + (int64_t)(j - 1) * C)) : z;
+      const float4 ga2 = nt > 1 && okj ? __ldg(reinterpret_cast<const float4*>(rb + (int64_t)j * C)) : z;
+      const float4 gb2 = nt > 1 && okj1 ? __ldg(reinterpret_cast<const float4*>(rb + (int64_t)(j - 1) * C)) : z;
+      float4 ae = z, ao = z;
+      if (nt > 0) {
+        if (okj) ae = fadd4(ae, fmul4(ga, wa[0]));    // kw = 0
+        if (okj1) ae = fadd4(ae, fmul4(gb, wa[2]));   // kw = 2
+        if (okj) ao = fadd4(ao, fmul4(ga, wa[1]));    // kw = 1
+      }
+      if (nt > 1) {
+        if (okj) ae = fadd4(ae, fmul4(ga2, wb[0]));
+        if (okj1) ae = fadd4(ae, fmul4(gb2, wb[2]));
+        if (okj) ao = fadd4(ao, fmul4(ga2, wb[1]));
+      }
+      const int we = 2 * j - a.pW, wo = we + 1;
+      if ((unsigned)we < (unsigned)a.W) *reinterpret_cast<float4*>(xrow + (int64_t)we * C) = ae;
+      if ((unsigned)wo < (unsigned)a.W) *reinterpret_cast<float4*>(xrow + (int64_t)wo * C) = ao;
+    }
+  };
+  for (int r = r0; r < r1; ++r) {
+    const int n = r / a.H, hi = r - n * a.H;
+    const int hn = hi + a.pH;
+    const float* gimg = dy + (int64_t)n * a.Ho * a.Wo * C + c;
+    float* xrow = dx + (int64_t)r * a.W * C + c;
+    if (hn & 1) {  // kh = 1 only
+      const int ho = hn >> 1;
+      if (ho < a.Ho) row(gimg, xrow, 1, ho, 0, wr + 3, wr + 3);
+      else row(gimg, xrow, 0, 0, 0, wr, wr);
+    } else {       // kh = 0 (ho = hn/2), then kh = 2 (ho = hn/2 - 1)
+      const int ho0 = hn >> 1, ho2 = ho0 - 1;
+      const bool v0 = ho0 < a.Ho, v2 = ho2 >= 0 && ho2 < a.Ho;
+      if (v0 && v2) row(gimg, xrow, 2, ho0, ho2, wr, wr + 6);
+      else if (v0) row(gimg, xrow, 1, ho0, 0, wr, wr);
+      else if (v2) row(gimg, xrow, 1, ho2, 0, wr + 6, wr + 6);
+      else row(gimg, xrow, 0, 0, 0, wr, wr);
+    }
+  }
+}
+
 // depthwise_conv2d_kernels.cl:59-104, any dm / C.
 __global__ void __launch_bounds__(kThreads) dw_dgrad_scalar_kernel(const float* __restrict__ dy,
                                                                     const float* __restrict__ w,
@@ -616,8 +684,21 @@ int b2_depthwise_conv2d_backprop_input(b2_stream_t stream, const int32_t input_s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const DwArgs a = to_args(g);
   if (g.dm == 1 && g.Ci % 4 == 0 && aligned16(out_backprop) && aligned16(filter) && aligned16(output)) {
-    dw_dgrad_rows_kernel<<<(unsigned)(g.N * g.H), row_block((int)(g.Ci / 4), g.W), 0, s>>>(out_backprop, filter,
-                                                                                          output, a);
+    if (g.kH == 3 && g.kW == 3 && g.sH == 2 && g.sW == 2) {
+      const int pairs = (int)((g.W + g.pW + 1) / 2);
+      const dim3 blk = row_block((int)(g.Ci / 4), pairs);
+      const int64_t chunks = ceil_div(g.Ci / 4, (int64_t)blk.x);
+      const int64_t rows = g.N * g.H;
+      int64_t want = (int64_t)d->sm_count * 16 / chunks;
+      if (want < 1) want = 1;
+      int64_t rpb = ceil_div(rows, want);
+      if (rpb > 8) rpb = 8;
+      const dim3 grid((unsigned)ceil_div(rows, rpb), (unsigned)chunks);
+      dw_dgrad_s2k3_kernel<<<grid, blk, 0, s>>>(out_backprop, filter, output, a, pairs, (int)rpb);
+    } else {
+      dw_dgrad_rows_kernel<<<(unsigned)(g.N * g.H), row_block((int)(g.Ci / 4), g.W), 0, s>>>(out_backprop, filter,
+                                                                                            output, a);
+    }
   } else {
     dw_dgrad_scalar_kernel<<<grid_for(g.in_elems(), kThreads, 8), kThreads, 0, s>>>(out_backprop, filter,
                                                                                     output, a);

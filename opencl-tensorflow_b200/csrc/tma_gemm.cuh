@@ -397,14 +397,22 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
       int wo = k - ro * cr.Wo;
       int b = (ro - k0 / cr.Wo) * cr.sH * cr.wcp + wo * cr.sW * cr.Ci;
       const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
+      if (cr.Wo >= 16) {
+        // at most one row change in 16 pixels: every offset is independent of
+        // the previous one, so the 16 loads can all be in flight
+        const int n1 = cr.Wo - wo;  // pixels left in the first output row
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] = mok ? base[b] : 0.0f;
-        if (++wo == cr.Wo) {
-          wo = 0;
-          b += wrap;
-        } else {
-          b += step;
+        for (int i = 0; i < 16; ++i) v[i] = mok ? base[b + i * step + (i >= n1 ? wrap - step : 0)] : 0.0f;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v[i] = mok ? base[b] : 0.0f;
+          if (++wo == cr.Wo) {
+            wo = 0;
+            b += wrap;
+          } else {
+            b += step;
+          }
         }
       }
     }

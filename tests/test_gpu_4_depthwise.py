@@ -84,3 +84,16 @@ def test_dwconv2d_filter_grad_tall_and_wide_taps(otf, port, shape_x, ws, st, pad
     dy = np.random.default_rng(10).standard_normal(ry.shape).astype(np.float32)
     dw = otf.depthwise_conv2d_backprop_filter(_cuda(x), list(ws), _cuda(dy), strides=st, padding=padding)
     assert_close(to_np(dw), port.depthwise_conv2d_backprop_filter(x, ws, dy, st, padding), what="dw")
+
+
+@pytest.mark.parametrize("shape_x,padding", [((2, 30, 33, 4), "VALID"), ((3, 11, 10, 8), "VALID"),
+                                             ((2, 11, 13, 12), "SAME"), ((4, 16, 8, 96), "SAME")])
+def test_dwconv2d_input_grad_3x3_stride2(otf, port, shape_x, padding):
+    """3x3 stride-2 input gradients (the column-pair kernel), including input
+    rows and columns that no tap reaches: bit-exact with the reference."""
+    x, w = _inputs(12, shape_x, (3, 3, shape_x[3], 1))
+    st = (1, 2, 2, 1)
+    ry = port.depthwise_conv2d(x, w, st, padding)
+    dy = np.random.default_rng(13).standard_normal(ry.shape).astype(np.float32)
+    dx = otf.depthwise_conv2d_backprop_input(list(shape_x), _cuda(w), _cuda(dy), strides=st, padding=padding)
+    assert_bitexact(to_np(dx), port.depthwise_conv2d_backprop_input(shape_x, w, dy, st, padding), "dx")
