@@ -85,6 +85,63 @@ __global__ void __launch_bounds__(kThreads) dw_fwd_vec4_kernel(const float* __re
   }
 }
 
+// depthwise_conv2d_kernels.cl:16-56 for the 3x3, stride-2 case (dm == 1,
+// C % 4 == 0): thread (x, y) of CTA (output-row band, channel chunk) produces
+// output columns 2j and 2j + 1 of each row of the band for its 4 channels from
+// the five input columns they share (15 loads instead of 18, all issued
+// before the adds), the filter in registers; taps are added in the
+// reference's (kh, kw) order with round-to-nearest multiply and add, out-of-
+// image taps skipped.
+__global__ void __launch_bounds__(kThreads) dw_fwd_s2k3_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ w, float* __restrict__ y,
+                                                                DwArgs a, int pairs, int rows_per_block) {
+  const int c4 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c4 >= (a.C >> 2)) return;
+  const int C = a.C, c = 4 * c4;
+  float4 wr[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) wr[k] = __ldg(reinterpret_cast<const float4*>(w + k * C + c));
+  const int rows = a.N * a.Ho;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = r0; r < r1; ++r) {
+    const int n = r / a.Ho, ho = r - n * a.Ho;
+    const int hi0 = 2 * ho - a.pH;
+    const float* ximg = x + (int64_t)n * a.H * a.W * C + c;
+    float* yrow = y + (int64_t)r * a.Wo * C + c;
+    for (int j = threadIdx.y; j < pairs; j += blockDim.y) {
+      const int wi0 = 4 * j - a.pW;  // first input column of output 2j
+      float4 v[3][5];
+      bool okr[3], okc[5];
+#pragma unroll
+      for (int q = 0; q < 5; ++q) okc[q] = (unsigned)(wi0 + q) < (unsigned)a.W;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+        const int hi = hi0 + kh;
+        okr[kh] = (unsigned)hi < (unsigned)a.H;
+        const float* xr = ximg + (int64_t)hi * a.W * C;
+#pragma unroll
+        for (int q = 0; q < 5; ++q)
+          v[kh][q] = okr[kh] && okc[q] ? __ldg(reinterpret_cast<const float4*>(xr + (int64_t)(wi0 + q) * C)) : z;
+      }
+      float4 a0 = z, a1 = z;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+        if (!okr[kh]) continue;
+#pragma unroll
+        for (int kw = 0; kw < 3; ++kw) {
+          if (okc[kw]) a0 = fadd4(a0, fmul4(v[kh][kw], wr[kh * 3 + kw]));
+          if (okc[kw + 2]) a1 = fadd4(a1, fmul4(v[kh][kw + 2], wr[kh * 3 + kw]));
+        }
+      }
+      const int wo0 = 2 * j;
+      if (wo0 < a.Wo) *reinterpret_cast<float4*>(yrow + (int64_t)wo0 * C) = a0;
+      if (wo0 + 1 < a.Wo) *reinterpret_cast<float4*>(yrow + (int64_t)(wo0 + 1) * C) = a1;
+    }
+  }
+}
+
 // depthwise_conv2d_kernels.cl:16-56, any dm / C.
 __global__ void __launch_bounds__(kThreads) dw_fwd_scalar_kernel(const float* __restrict__ x,
                                                                   const float* __restrict__ w,
@@ -655,7 +712,20 @@ int b2_depthwise_conv2d(b2_stream_t stream, const float* input, const int64_t in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const DwArgs a = to_args(g);
   if (g.dm == 1 && g.Ci % 4 == 0 && aligned16(input) && aligned16(filter) && aligned16(output)) {
-    dw_fwd_vec4_kernel<<<grid_for(g.out_elems() / 4, kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
+    if (g.kH == 3 && g.kW == 3 && g.sH == 2 && g.sW == 2) {
+      const int pairs = (int)((g.Wo + 1) / 2);
+      const dim3 blk = row_block((int)(g.Ci / 4), pairs);
+      const int64_t chunks = ceil_div(g.Ci / 4, (int64_t)blk.x);
+      const int64_t rows = g.N * g.Ho;
+      int64_t want = (int64_t)d->sm_count * 16 / chunks;
+      if (want < 1) want = 1;
+      int64_t rpb = ceil_div(rows, want);
+      if (rpb > 8) rpb = 8;
+      const dim3 grid((unsigned)ceil_div(rows, rpb), (unsigned)chunks);
+      dw_fwd_s2k3_kernel<<<grid, blk, 0, s>>>(input, filter, output, a, pairs, (int)rpb);
+    } else {
+      dw_fwd_vec4_kernel<<<grid_for(g.out_elems() / 4, kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
+    }
   } else {
     dw_fwd_scalar_kernel<<<grid_for(g.out_elems(), kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
   }

@@ -88,12 +88,15 @@ def test_dwconv2d_filter_grad_tall_and_wide_taps(otf, port, shape_x, ws, st, pad
 
 @pytest.mark.parametrize("shape_x,padding", [((2, 30, 33, 4), "VALID"), ((3, 11, 10, 8), "VALID"),
                                              ((2, 11, 13, 12), "SAME"), ((4, 16, 8, 96), "SAME")])
-def test_dwconv2d_input_grad_3x3_stride2(otf, port, shape_x, padding):
-    """3x3 stride-2 input gradients (the column-pair kernel), including input
-    rows and columns that no tap reaches: bit-exact with the reference."""
+def test_dwconv2d_3x3_stride2_column_pairs(otf, port, shape_x, padding):
+    """3x3 stride-2 forward and input gradient (the column-pair kernels),
+    including odd widths, padding taps and input rows and columns that no tap
+    reaches: bit-exact with the reference."""
     x, w = _inputs(12, shape_x, (3, 3, shape_x[3], 1))
     st = (1, 2, 2, 1)
     ry = port.depthwise_conv2d(x, w, st, padding)
+    y = otf.depthwise_conv2d(_cuda(x), _cuda(w), strides=st, padding=padding)
+    assert_bitexact(to_np(y), ry, "fwd")
     dy = np.random.default_rng(13).standard_normal(ry.shape).astype(np.float32)
     dx = otf.depthwise_conv2d_backprop_input(list(shape_x), _cuda(w), _cuda(dy), strides=st, padding=padding)
     assert_bitexact(to_np(dx), port.depthwise_conv2d_backprop_input(shape_x, w, dy, st, padding), "dx")
