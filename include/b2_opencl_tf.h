@@ -214,13 +214,18 @@ int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* x,
 /* OpenclBatchNormTraining followed by OpenclRelu on its output, in one call:
  * z = relu(BN(x)) with the statistics of b2_batch_norm_training; z is bit-for-
  * bit the two ops in sequence (src/ops/batchnorm_ops.cc:87-180 then
- * src/ops/relu_ops.cc), with one pass over x and no intermediate tensor.  Not
- * an op of the reference: the fusion of the pair its layers run back to back. */
+ * src/ops/relu_ops.cc), with one pass over x and no intermediate tensor.  When
+ * moving_mean / moving_var are not NULL it also applies the layer's
+ * moving-average update exactly as b2_batch_norm_update_moving would (same
+ * rounding), in the statistics pass.  Not an op of the reference: the fusion
+ * of the pair its layers run back to back. */
 int b2_batch_norm_relu_training(b2_stream_t stream, const float* x,
                                 const int64_t x_shape[4], const float* gamma,
                                 int64_t gamma_len, const float* beta,
                                 int64_t beta_len, float epsilon, float* z,
-                                float* saved_mean, float* saved_var);
+                                float* saved_mean, float* saved_var,
+                                float* moving_mean, float* moving_var,
+                                float momentum, float one_minus_momentum);
 
 /* The gradient of b2_batch_norm_relu_training: OpenclReluGrad followed by
  * OpenclBatchNormGrad (src/ops/relu_ops.cc, src/ops/batchnorm_ops.cc:313-416)

@@ -241,11 +241,13 @@ __device__ __forceinline__ float2 sum_partials(const float2* __restrict__ partia
 
 // Stage 2 of the statistics: mean = sum / NHW, var = sum_sq / NHW - mean^2
 // (the reference's formula), inv_std = 1 / sqrt(var + eps).
-__global__ void __launch_bounds__(kFinThreads) bn_stats_finalize_kernel(const float2* __restrict__ partial,
-                                                                        int blocks, int C, int64_t nhw, float eps,
-                                                                        float* __restrict__ mean,
-                                                                        float* __restrict__ var,
-                                                                        float* __restrict__ inv_std) {
+// With moving_mean != nullptr also the layer's moving-average update (as
+// bn_moving_update_kernel: momentum * moving + one_minus_momentum * batch,
+// each product and the sum rounded to fp32).
+__global__ void __launch_bounds__(kFinThreads) bn_stats_finalize_kernel(
+    const float2* __restrict__ partial, int blocks, int C, int64_t nhw, float eps, float* __restrict__ mean,
+    float* __restrict__ var, float* __restrict__ inv_std, float* __restrict__ moving_mean = nullptr,
+    float* __restrict__ moving_var = nullptr, float momentum = 0.0f, float one_minus_momentum = 0.0f) {
   const int c = blockIdx.x;
   const float2 s = sum_partials(partial, blocks, C, c);
   if (threadIdx.x == 0) {
@@ -255,6 +257,10 @@ __global__ void __launch_bounds__(kFinThreads) bn_stats_finalize_kernel(const fl
     mean[c] = m;
     var[c] = v;
     inv_std[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v, eps)));
+    if (moving_mean) {
+      moving_mean[c] = __fadd_rn(__fmul_rn(momentum, moving_mean[c]), __fmul_rn(one_minus_momentum, m));
+      moving_var[c] = __fadd_rn(__fmul_rn(momentum, moving_var[c]), __fmul_rn(one_minus_momentum, v));
+    }
   }
 }
 
@@ -484,7 +490,8 @@ int launch_normalize(cudaStream_t s, const float* x, const float* mean, const fl
 // Training forward: statistics, then y = BN(x) (relu: y = relu(BN(x))).
 int bn_training(cudaStream_t s, const float* x, const int64_t* x_shape, const float* gamma, int64_t gamma_len,
                 const float* beta, int64_t beta_len, float epsilon, float* y, float* saved_mean, float* saved_var,
-                bool relu) {
+                bool relu, float* moving_mean = nullptr, float* moving_var = nullptr, float momentum = 0.0f,
+                float one_minus_momentum = 0.0f) {
   B2_RETURN_IF_ERROR(validate_nhwc(x_shape, "x"));
   const int64_t C = x_shape[3];
   B2_REQUIRE(gamma_len == C && beta_len == C, "gamma/beta size must equal channels");
@@ -503,7 +510,8 @@ int bn_training(cudaStream_t s, const float* x, const int64_t* x_shape, const fl
   B2_RETURN_IF_ERROR(launch_partials(s, 0, x, nullptr, nullptr, nullptr, epsilon, rows, (int)C, vec_ok, d,
                                      part.as<float2>(), &used_blocks));
   bn_stats_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
-                                                                epsilon, saved_mean, saved_var, inv.as<float>());
+                                                                epsilon, saved_mean, saved_var, inv.as<float>(),
+                                                                moving_mean, moving_var, momentum, one_minus_momentum);
   B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
   if (total == 0) return B2_OK;
   return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok, relu);
@@ -580,10 +588,12 @@ int b2_batch_norm_training(b2_stream_t stream, const float* x, const int64_t x_s
 // src/ops/relu_ops.cc), one pass over x less and no intermediate tensor.
 int b2_batch_norm_relu_training(b2_stream_t stream, const float* x, const int64_t x_shape[4], const float* gamma,
                                 int64_t gamma_len, const float* beta, int64_t beta_len, float epsilon, float* z,
-                                float* saved_mean, float* saved_var) {
+                                float* saved_mean, float* saved_var, float* moving_mean, float* moving_var,
+                                float momentum, float one_minus_momentum) {
   clear_error();
+  B2_REQUIRE((moving_mean == nullptr) == (moving_var == nullptr), "moving_mean and moving_var go together");
   return bn_training(static_cast<cudaStream_t>(stream), x, x_shape, gamma, gamma_len, beta, beta_len, epsilon, z,
-                     saved_mean, saved_var, true);
+                     saved_mean, saved_var, true, moving_mean, moving_var, momentum, one_minus_momentum);
 }
 
 // src/ops/batchnorm_ops.cc:213-275

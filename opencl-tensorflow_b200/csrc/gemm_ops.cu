@@ -32,16 +32,30 @@ unsigned int dw_timeouts();  // depthwise.cu
 
 namespace tc {
 
-__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N,
-                                     const float* __restrict__ bias, float* __restrict__ out, int64_t ldo) {
+// D = sum_z P[z] (+ bias) in a fixed order: CTA (32 elements x kRedParts);
+// part j adds splits j, j + kRedParts, ... in order, then the parts are added
+// in part order -- deterministic, with all of a CTA's loads in flight at once.
+constexpr int kRedParts = 16;
+__global__ void __launch_bounds__(32 * kRedParts) splitk_reduce_kernel(const float* __restrict__ part, int splits,
+                                                                       int64_t M, int64_t N,
+                                                                       const float* __restrict__ bias,
+                                                                       float* __restrict__ out, int64_t ldo) {
+  __shared__ float s_part[kRedParts][32];
   const int64_t total = M * N;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    float s = 0.0f;
-    for (int z = 0; z < splits; ++z) s += part[(int64_t)z * total + i];
+  const int64_t i = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float acc = 0.0f;
+  if (i < total) {
+#pragma unroll 4
+    for (int z = threadIdx.y; z < splits; z += kRedParts) acc += __ldg(part + (int64_t)z * total + i);
+  }
+  s_part[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && i < total) {
+    float sum = s_part[0][threadIdx.x];
+    for (int j = 1; j < kRedParts; ++j) sum += s_part[j][threadIdx.x];
     const int64_t m = i / N, n = i - m * N;
-    if (bias) s += bias[n];
-    out[m * ldo + n] = s;
+    if (bias) sum += bias[n];
+    out[m * ldo + n] = sum;
   }
 }
 
@@ -492,7 +506,7 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   }
   B2_RETURN_IF_ERROR(rc);
   if (splits == 1) return B2_OK;
-  splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
   return check_launch(s, "splitk_reduce");
 }
 
@@ -551,7 +565,7 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
   B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)splits * M * N, s));
   prob.ep = Epilogue{part.as<float>(), N, nullptr, true};
   B2_RETURN_IF_ERROR(launch_gemm(prob, bn, s, name));
-  splitk_reduce_kernel<<<grid_for(M * N, 256, 8), 256, 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
   return check_launch(s, "splitk_reduce");
 }
 
@@ -562,7 +576,7 @@ __global__ void dense_bias_grad_kernel(const float* __restrict__ dy, int64_t bat
   const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= out_f) return;
   float acc = 0.0f;
-  constexpr int kAhead = 16;  // loads issued ahead of the in-order adds
+  constexpr int kAhead = 64;  // loads issued ahead of the in-order adds
   int64_t n = 0;
   for (; n + kAhead <= batch; n += kAhead) {
     float v[kAhead];

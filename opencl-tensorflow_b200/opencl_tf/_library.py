@@ -71,7 +71,7 @@ _SIGS = {
     "b2_batch_norm_inference": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _F32, _P],
     "b2_batch_norm_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
     "b2_batch_norm_update_moving": [_P, _P, _P, _P, _P, _I64, _F32, _F32],
-    "b2_batch_norm_relu_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P],
+    "b2_batch_norm_relu_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P, _P, _P, _F32, _F32],
     "b2_batch_norm_relu_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
     "b2_dense": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_backprop_input": [_P, _P, _P, _P, _P, _P],
@@ -333,7 +333,8 @@ def batch_norm_update_moving(moving_mean, moving_var, batch_mean, batch_var, mom
                                                 float(1.0 - momentum)))
 
 
-def _k_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3):
+def _k_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3, moving=None):
+    """moving: optional (moving_mean, moving_var, momentum), updated in place."""
     x = _input(x, "x")
     g = _input(gamma, "gamma")
     b = _input(beta, "beta")
@@ -342,9 +343,19 @@ def _k_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3):
     z = torch.empty_like(x)
     mean = torch.empty(C, device=x.device, dtype=torch.float32)
     var = torch.empty(C, device=x.device, dtype=torch.float32)
+    mm = mv = None
+    mom = 0.0
+    if moving is not None:
+        mm, mv, mom = moving
+        for t in (mm, mv):
+            if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous() and t.numel() == C):
+                raise errors.InvalidArgumentError("moving statistics must be contiguous fp32 CUDA vectors of C")
     with _on_device(x):
         _check(_lib.b2_batch_norm_relu_training(_stream(x), _p(x), _I64x4(*x.shape), _p(g), g.numel(), _p(b),
-                                                b.numel(), float(epsilon), _p(z), _p(mean), _p(var)))
+                                                b.numel(), float(epsilon), _p(z), _p(mean), _p(var),
+                                                _p(mm) if mm is not None else None,
+                                                _p(mv) if mv is not None else None, float(mom),
+                                                float(1.0 - mom)))
     return z, mean, var
 
 
@@ -625,9 +636,14 @@ raw_ops = _mk_raw_ops()
 def _mk_fused_ops():
     ns = types.SimpleNamespace()
 
-    def opencl_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3):
-        return _apply("OpenclBatchNormReluTraining", _k_batch_norm_relu_training, (x, gamma, beta),
-                      {"epsilon": float(epsilon)}, nondiff=(1, 2))
+    def opencl_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3, moving=None):
+        """moving: optional (moving_mean, moving_var, momentum) updated in the
+        statistics pass with the layer's EMA (same rounding as the layer)."""
+        attrs = {"epsilon": float(epsilon)}
+        if moving is not None:
+            attrs["moving"] = moving
+        return _apply("OpenclBatchNormReluTraining", _k_batch_norm_relu_training, (x, gamma, beta), attrs,
+                      nondiff=(1, 2))
 
     def opencl_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, epsilon=1e-3):
         return _k_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, float(epsilon))

@@ -172,11 +172,10 @@ class OpenCLBatchNormalization(_Layer):
         if training is None:
             training = self.training
         if bool(training):
-            z, batch_mean, batch_var = _library.fused_ops.opencl_batch_norm_relu_training(x, self.gamma, self.beta,
-                                                                               epsilon=self.epsilon)
-            with torch.no_grad():
-                _library.batch_norm_update_moving(self.moving_mean, self.moving_var, batch_mean.detach(),
-                                                  batch_var.detach(), self.momentum)
+            # the moving-average update runs in the op's statistics pass
+            z, _mean, _var = _library.fused_ops.opencl_batch_norm_relu_training(
+                x, self.gamma, self.beta, epsilon=self.epsilon,
+                moving=(self.moving_mean, self.moving_var, self.momentum))
             return z
         return relu(self.forward(x, training=False))
 
