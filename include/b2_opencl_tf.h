@@ -321,6 +321,42 @@ int b2_upsampling_coords(b2_stream_t stream, int32_t in_size,
                          int32_t out_size, int32_t* lo, int32_t* hi,
                          float* frac);
 
+/* ---- The training step around the ops ----------------------------------
+ * The reference trains with model.compile(optimizer=tf.keras.optimizers.Adam(
+ * 1e-3), loss="mse") (README.md:188-196); loss and optimizer are stock
+ * TensorFlow (2.10-2.15) host ops.  These entries replace them on the device;
+ * they are not ops of the reference's kernel library. */
+
+/* Keras "mse" for one batch: *loss = sum((pred - target)^2) / num_elements
+ * (the mean over the last axis, then over the batch, is the same mean).  One
+ * cluster of 8 CTAs, deterministic; `loss` is a device float. */
+int b2_mse_loss(b2_stream_t stream, const float* pred, const float* target,
+                int64_t num_elements, float* loss);
+
+/* Gradient of b2_mse_loss: grad_pred = (pred - target) * (2 * grad_loss /
+ * num_elements), grad_loss a device float (the upstream gradient). */
+int b2_mse_loss_grad(b2_stream_t stream, const float* pred,
+                     const float* target, int64_t num_elements,
+                     const float* grad_loss, float* grad_pred);
+
+/* Keras Adam's update of num_tensors parameter tensors (params[i], grads[i],
+ * m[i], v[i]: device fp32 arrays of sizes[i] elements; the pointer arrays are
+ * host memory), keras/optimizers/adam.py (TF 2.11+) / ApplyAdam (TF 2.10):
+ *   t = *iterations + 1,  alpha = lr * sqrt(1 - beta_2^t) / (1 - beta_1^t)
+ *   m += (g - m) * one_minus_beta_1;  v += (g*g - v) * one_minus_beta_2
+ *   p -= (m * alpha) / (sqrt(v) + epsilon)
+ * then *iterations = t.  one_minus_beta_* are passed as the caller rounds
+ * them (Keras: 1 - beta in double, then fp32).  `iterations` (int64) and
+ * `ticket` (uint32, zero before the first call; the kernel leaves it zero)
+ * are device memory owned by the optimizer, so the update replays correctly
+ * from a captured CUDA graph.  Calls sharing one ticket must be ordered. */
+int b2_adam_update(b2_stream_t stream, int num_tensors, float* const* params,
+                   const float* const* grads, float* const* m,
+                   float* const* v, const int64_t* sizes,
+                   float learning_rate, float beta_1, float beta_2,
+                   float one_minus_beta_1, float one_minus_beta_2,
+                   float epsilon, int64_t* iterations, unsigned int* ticket);
+
 /* Number of bounded device-side waits (tensor-core pipeline barriers) that
  * expired since the library was loaded; synchronise the stream first.  A
  * nonzero count means a kernel gave up waiting and its output is invalid. */

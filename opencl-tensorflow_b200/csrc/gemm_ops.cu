@@ -569,24 +569,36 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
   return check_launch(s, "splitk_reduce");
 }
 
-// dense_kernels.cl:88-102: db[o] = sum_n dy[n, o], one thread per column in
-// the reference's order (bit-identical result).
-__global__ void dense_bias_grad_kernel(const float* __restrict__ dy, int64_t batch, int64_t out_f,
-                                       float* __restrict__ db) {
-  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (o >= out_f) return;
+// dense_kernels.cl:88-102: db[o] = sum_n dy[n, o], added in the reference's
+// order (n ascending, one serial sum per column: bit-identical result).  A CTA
+// owns kBiasCols columns; its eight warps stage kBiasRows rows of them in
+// shared memory with independent coalesced loads, then warp 0 adds each
+// column's staged values in order.  The loads are off the serial chain, which
+// is what bounds a one-thread-per-column loop over global memory.
+constexpr int kBiasCols = 32;
+constexpr int kBiasRows = 256;
+constexpr int kBiasThreads = 256;
+
+__global__ void __launch_bounds__(kBiasThreads) dense_bias_grad_kernel(const float* __restrict__ dy, int64_t batch,
+                                                                        int64_t out_f, float* __restrict__ db) {
+  __shared__ float tile[kBiasRows][kBiasCols];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t o = (int64_t)blockIdx.x * kBiasCols + lane;
+  const bool col_ok = o < out_f;
   float acc = 0.0f;
-  constexpr int kAhead = 64;  // loads issued ahead of the in-order adds
-  int64_t n = 0;
-  for (; n + kAhead <= batch; n += kAhead) {
-    float v[kAhead];
-#pragma unroll
-    for (int i = 0; i < kAhead; ++i) v[i] = __ldg(dy + (n + i) * out_f + o);
-#pragma unroll
-    for (int i = 0; i < kAhead; ++i) acc = __fadd_rn(acc, v[i]);
+  for (int64_t n0 = 0; n0 < batch; n0 += kBiasRows) {
+    const int rows = (int)(batch - n0 < kBiasRows ? batch - n0 : kBiasRows);
+#pragma unroll 8
+    for (int r = warp; r < rows; r += kBiasThreads / 32)
+      tile[r][lane] = col_ok ? __ldg(dy + (n0 + r) * out_f + o) : 0.0f;
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll 16
+      for (int r = 0; r < rows; ++r) acc = __fadd_rn(acc, tile[r][lane]);
+    }
+    __syncthreads();
   }
-  for (; n < batch; ++n) acc = __fadd_rn(acc, __ldg(dy + n * out_f + o));
-  db[o] = acc;
+  if (warp == 0 && col_ok) db[o] = acc;
 }
 
 int conv_geom_fwd(const int64_t* input_shape, const int64_t* filter_shape, const int32_t* strides,
@@ -768,7 +780,9 @@ int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dense_bias_grad_kernel<<<(unsigned)ceil_div(out_f, 32), 32, 0, s>>>(grad_y, batch, out_f, grad_b);
+  B2_REQUIRE(ceil_div(out_f, kBiasCols) <= kMaxInt32, "dense_backprop_bias: too many output features");
+  dense_bias_grad_kernel<<<(unsigned)ceil_div(out_f, kBiasCols), kBiasThreads, 0, s>>>(grad_y, batch, out_f,
+                                                                                        grad_b);
   return check_launch(s, "dense_backprop_bias");
 }
 

@@ -186,6 +186,63 @@ __global__ void __launch_bounds__(kThreads) up_bwd_kernel(const float* __restric
   }
 }
 
+// The same gather with one CTA per image: the image's dy (Ho*Wo*C floats) and
+// both axes' corner coordinates are staged in shared memory first, so the
+// per-element walk (same candidates, same order, same arithmetic as
+// up_bwd_kernel<1>, hence the same bits) reads shared memory only.  Used when
+// the image fits kStagedSmemBytes -- the small heads this op closes networks
+// with, where the global-memory walk was latency-bound at a few warps per SM.
+constexpr int kStagedSmemBytes = 48 * 1024;
+
+__global__ void __launch_bounds__(kThreads) up_bwd_staged_kernel(const float* __restrict__ dy,
+                                                                  float* __restrict__ dx, UpArgs a, int sy, int sx,
+                                                                  int vec_copy) {
+  extern __shared__ float4 smem_v[];
+  float* sdy = reinterpret_cast<float*>(smem_v);
+  const int64_t img = (int64_t)a.Ho * a.Wo * a.C;
+  Coord* rows = reinterpret_cast<Coord*>(sdy + img);
+  Coord* cols = rows + a.Ho;
+  const int n = blockIdx.x;
+  const float* src = dy + (int64_t)n * img;
+  if (vec_copy) {
+    for (int64_t i = threadIdx.x; i < img / 4; i += kThreads)
+      smem_v[i] = reinterpret_cast<const float4*>(src)[i];
+  } else {
+    for (int64_t i = threadIdx.x; i < img; i += kThreads) sdy[i] = src[i];
+  }
+  for (int o = threadIdx.x; o < a.Ho; o += kThreads) rows[o] = up_coord(o, a.H, a.Ho);
+  for (int o = threadIdx.x; o < a.Wo; o += kThreads) cols[o] = up_coord(o, a.W, a.Wo);
+  __syncthreads();
+  const int per_img = a.H * a.W * a.C;
+  float* out = dx + (int64_t)n * per_img;
+  for (int e = threadIdx.x; e < per_img; e += kThreads) {
+    const int c = e % a.C;
+    const int p = e / a.C;
+    const int iw = p % a.W, ih = p / a.W;
+    const int oh_lo = max(0, (ih - 1) * sy - 1), oh_hi = min(a.Ho - 1, (ih + 2) * sy);
+    const int ow_lo = max(0, (iw - 1) * sx - 1), ow_hi = min(a.Wo - 1, (iw + 2) * sx);
+    float acc = 0.0f;
+    for (int oh = oh_lo; oh <= oh_hi; ++oh) {
+      const Coord ch = rows[oh];
+      const bool h0 = ch.lo == ih, h1 = ch.hi == ih;
+      if (!h0 && !h1) continue;
+      const float a_h = __fsub_rn(1.0f, ch.frac);
+      for (int ow = ow_lo; ow <= ow_hi; ++ow) {
+        const Coord cw = cols[ow];
+        const bool w0 = cw.lo == iw, w1 = cw.hi == iw;
+        if (!w0 && !w1) continue;
+        const float g = sdy[((int64_t)oh * a.Wo + ow) * a.C + c];
+        const float b_w = __fsub_rn(1.0f, cw.frac);
+        if (h0 && w0) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(a_h, b_w), g));
+        if (h0 && w1) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(a_h, cw.frac), g));
+        if (h1 && w0) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(ch.frac, b_w), g));
+        if (h1 && w1) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(ch.frac, cw.frac), g));
+      }
+    }
+    out[e] = acc;
+  }
+}
+
 __global__ void up_coords_kernel(int in, int out, int* lo, int* hi, float* frac) {
   const int o = blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= out) return;
@@ -260,7 +317,13 @@ int b2_upsampling_bilinear2d_grad(b2_stream_t stream, const float* grad_out, con
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (a.C % 4 == 0 && aligned16(grad_out) && aligned16(grad_in))
+  const int64_t staged_bytes = out_total / (a.N > 0 ? a.N : 1) * 4 + (int64_t)(a.Ho + a.Wo) * (int64_t)sizeof(Coord);
+  if (staged_bytes <= kStagedSmemBytes) {
+    const int64_t img = (int64_t)a.Ho * a.Wo * a.C;
+    const int vec_copy = img % 4 == 0 && aligned16(grad_out);
+    // the coordinate tables start after the image, on a 4-byte boundary
+    up_bwd_staged_kernel<<<a.N, kThreads, (size_t)staged_bytes, s>>>(grad_out, grad_in, a, sy, sx, vec_copy);
+  } else if (a.C % 4 == 0 && aligned16(grad_out) && aligned16(grad_in))
     up_bwd_kernel<4><<<grid_for(in_total / 4, kThreads, 8), kThreads, 0, s>>>(grad_out, grad_in, a, sy, sx);
   else
     up_bwd_kernel<1><<<grid_for(in_total, kThreads, 8), kThreads, 0, s>>>(grad_out, grad_in, a, sy, sx);

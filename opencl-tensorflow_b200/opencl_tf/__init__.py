@@ -16,9 +16,14 @@ _bias), upsampling_bilinear_2d (+ grad).
 Layers (``opencl_tf.layers``): OpenCLConv2D, OpenCLDepthwiseConv2D,
 OpenCLBatchNormalization, OpenCLReLU, OpenCLSigmoid, OpenCLDense,
 OpenCLUpSampling2D.
+
+Beyond the reference's op set: ``fused_ops`` (BatchNorm -> ReLU in one op),
+``step_ops`` (the MSE loss of the training recipe) and ``optimizers.Adam``
+(Keras Adam as one multi-tensor kernel); ``train.TrainStep`` runs the whole
+training step from one CUDA graph.
 """
 
-from ._library import raw_ops, init, pool_stats, pool_trim, device_timeouts, library_path
+from ._library import raw_ops, fused_ops, step_ops, init, pool_stats, pool_trim, device_timeouts, library_path
 from .ops import (
     conv2d,
     conv2d_backprop_input,
@@ -43,6 +48,7 @@ from .ops import (
 from . import errors  # noqa: F401
 from . import gradients  # noqa: F401  -- registers the gradient functions
 from . import layers  # noqa: F401
+from . import optimizers  # noqa: F401
 
 __all__ = [
     "raw_ops",
@@ -53,6 +59,7 @@ __all__ = [
     "sigmoid", "sigmoid_grad",
     "dense", "dense_backprop_input", "dense_backprop_weight", "dense_backprop_bias",
     "upsampling_bilinear_2d", "upsampling_bilinear_2d_grad",
+    "fused_ops", "step_ops", "optimizers",
     "layers", "errors", "init", "pool_stats", "pool_trim", "device_timeouts", "library_path",
 ]
 

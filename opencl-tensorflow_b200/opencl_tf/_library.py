@@ -80,6 +80,9 @@ _SIGS = {
     "b2_upsampling_bilinear2d": [_P, _P, _P, _P, _I, _P],
     "b2_upsampling_bilinear2d_grad": [_P, _P, _P, _P, _P, _I, _P],
     "b2_upsampling_coords": [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P],
+    "b2_mse_loss": [_P, _P, _P, _I64, _P],
+    "b2_mse_loss_grad": [_P, _P, _P, _I64, _P, _P],
+    "b2_adam_update": [_P, _I, _P, _P, _P, _P, _P, _F32, _F32, _F32, _F32, _F32, _F32, _P, _P],
     "b2_pool_trim": [],
     "b2_device_timeouts": [ctypes.POINTER(ctypes.c_uint)],
     "b2_kernel_launch_count": [ctypes.POINTER(ctypes.c_uint64)],
@@ -456,6 +459,71 @@ def _k_dense_backprop_bias(grad_y):
     return db
 
 
+def _pred_target(pred, target):
+    p = _input(pred, "y_pred")
+    t = _input(target, "y_true")
+    if p.shape != t.shape:
+        raise errors.InvalidArgumentError(
+            f"y_pred and y_true must have the same shape, got {tuple(p.shape)} and {tuple(t.shape)}")
+    if p.device != t.device:
+        raise errors.InvalidArgumentError("y_pred and y_true must live on the same device")
+    if p.numel() == 0:
+        raise errors.InvalidArgumentError("mean squared error of an empty batch is undefined")
+    return p, t
+
+
+def _k_mse_loss(pred, target):
+    p, t = _pred_target(pred, target)
+    loss = torch.empty((), device=p.device, dtype=torch.float32)
+    with _on_device(p):
+        _check(_lib.b2_mse_loss(_stream(p), _p(p), _p(t), p.numel(), _p(loss)))
+    return loss
+
+
+def _k_mse_loss_grad(pred, target, grad_loss):
+    p, t = _pred_target(pred, target)
+    g = _input(grad_loss, "grad_loss")
+    if g.numel() != 1 or g.device != p.device:
+        raise errors.InvalidArgumentError("grad_loss must be a scalar on the prediction's device")
+    out = torch.empty_like(p)
+    with _on_device(p):
+        _check(_lib.b2_mse_loss_grad(_stream(p), _p(p), _p(t), p.numel(), _p(g), _p(out)))
+    return out
+
+
+def adam_update(params, grads, ms, vs, learning_rate, beta_1, beta_2, epsilon, iterations, ticket):
+    """One Keras Adam update of every (param, grad, m, v) quadruple in one
+    multi-tensor launch (all fp32, contiguous, on one device); ``iterations``
+    (int64 scalar) and ``ticket`` (32-bit scalar, zero) are the optimizer's
+    device state.  ``1 - beta`` is rounded as Keras rounds it: in double, then
+    to fp32."""
+    n = len(params)
+    if not (len(grads) == len(ms) == len(vs) == n):
+        raise errors.InvalidArgumentError("params, grads, m and v must have the same length")
+    if n == 0:
+        return
+    dev = params[0].device
+    for group in (params, grads, ms, vs):
+        for t in group:
+            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+                    and t.device == dev):
+                raise errors.InvalidArgumentError(
+                    "Adam operands must be contiguous fp32 tensors on the parameters' CUDA device")
+    for a, b, c, d in zip(params, grads, ms, vs):
+        if not (a.numel() == b.numel() == c.numel() == d.numel()):
+            raise errors.InvalidArgumentError("a parameter, its gradient and its slots must have the same size")
+    if not (iterations.is_cuda and iterations.dtype == torch.int64 and iterations.device == dev and
+            ticket.is_cuda and ticket.element_size() == 4 and ticket.device == dev):
+        raise errors.InvalidArgumentError("iterations (int64) and ticket (32-bit) must live on the parameters' device")
+    arr = ctypes.c_void_p * n
+    with _on_device(params[0]):
+        _check(_lib.b2_adam_update(_stream(params[0]), n, arr(*(_p(t) for t in params)),
+                                   arr(*(_p(t) for t in grads)), arr(*(_p(t) for t in ms)),
+                                   arr(*(_p(t) for t in vs)), (_I64 * n)(*(t.numel() for t in params)),
+                                   float(learning_rate), float(beta_1), float(beta_2), float(1.0 - beta_1),
+                                   float(1.0 - beta_2), float(epsilon), _p(iterations), _p(ticket)))
+
+
 def _size_arr(size):
     s = [int(a) for a in size]
     return (ctypes.c_int32 * len(s))(*s), len(s)
@@ -656,6 +724,27 @@ def _mk_fused_ops():
 fused_ops = _mk_fused_ops()
 """Ops with no counterpart in the reference: pairs its layers run back to back
 (BatchNormTraining -> Relu), fused, with bit-identical results."""
+
+
+def _mk_step_ops():
+    ns = types.SimpleNamespace()
+
+    def opencl_mse_loss(y_pred, y_true):
+        """Keras "mse" of one batch as a device scalar (differentiable in
+        y_pred and y_true)."""
+        return _apply("OpenclMseLoss", _k_mse_loss, (y_pred, y_true), {})
+
+    def opencl_mse_loss_grad(y_pred, y_true, grad_loss):
+        return _k_mse_loss_grad(y_pred, y_true, grad_loss)
+
+    ns.opencl_mse_loss = opencl_mse_loss
+    ns.opencl_mse_loss_grad = opencl_mse_loss_grad
+    return ns
+
+
+step_ops = _mk_step_ops()
+"""The training step's loss on the device: stock Keras in the reference
+(``model.compile(loss="mse")``, README.md:188-196), not an op of its library."""
 
 
 # ------------------------------------------------------- runtime utilities

@@ -12,7 +12,9 @@ which tensors those ops receive --
 * Sigmoid: from the forward OUTPUT y;
 * Dense: three backward ops (input, weight, bias);
 * bilinear UpSampling2D: the backward op with the input's host shape;
-* BatchNorm (inference): no gradient (a LookupError if one is requested).
+* BatchNorm (inference): no gradient (a LookupError if one is requested);
+* the extensions: BatchNorm->ReLU (fused_ops) and the step's MSE loss
+  (step_ops), each with its own one-launch backward.
 
 An input whose gradient nobody needs gets no backward launch -- what TF's
 graph pruning does for ``model.fit`` -- so the network's first convolution
@@ -20,7 +22,7 @@ never computes a gradient for the image batch.
 """
 from __future__ import annotations
 
-from ._library import RegisterGradient, fused_ops, raw_ops
+from ._library import RegisterGradient, fused_ops, raw_ops, step_ops
 
 
 def _host_shape(t):
@@ -92,3 +94,11 @@ def _dense_grad(op, grad):
 @RegisterGradient("OpenclUpsamplingBilinear2d")
 def _upsampling_bilinear_grad(op, grad):
     return [raw_ops.opencl_upsampling_bilinear2d_grad(grad, _host_shape(op.inputs[0]), size=op.get_attr("size"))]
+
+
+@RegisterGradient("OpenclMseLoss")
+def _mse_loss_grad(op, grad):
+    y_pred, y_true = op.inputs
+    need_pred, need_true = op.needs_input_grad
+    g = step_ops.opencl_mse_loss_grad(y_pred, y_true, grad)
+    return [g if need_pred else None, g.neg() if need_true else None]

@@ -29,7 +29,7 @@ _KERNELS = ["_k_conv2d", "_k_conv2d_backprop_input", "_k_conv2d_backprop_filter"
             "_k_sigmoid", "_k_sigmoid_grad", "_k_batch_norm_training", "_k_batch_norm_inference",
             "_k_batch_norm_grad", "_k_dense", "_k_dense_backprop_input", "_k_dense_backprop_weight",
             "_k_dense_backprop_bias", "_k_upsampling_bilinear2d", "_k_upsampling_bilinear2d_grad",
-            "_k_batch_norm_relu_training", "_k_batch_norm_relu_grad"]
+            "_k_batch_norm_relu_training", "_k_batch_norm_relu_grad", "_k_mse_loss", "_k_mse_loss_grad"]
 
 
 def peaks(path=None) -> dict:

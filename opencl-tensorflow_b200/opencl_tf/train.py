@@ -1,7 +1,9 @@
 """One training step of a model built from this package: forward, MSE loss,
 backward through the registered gradients, data-parallel gradient averaging,
 Adam -- what ``model.compile(Adam(1e-3), "mse"); model.fit(...)`` runs per
-batch in the reference (README.md:188-196).
+batch in the reference (README.md:188-196).  Loss and optimizer are this
+package's device kernels with Keras's formulas (``step_ops.opencl_mse_loss``,
+``optimizers.Adam``).
 
 ``TrainStep(model, graphed=True)`` captures the whole step in one CUDA graph
 after a few eager warm-up steps, so a step costs one graph launch instead of
@@ -19,9 +21,14 @@ import torch
 import torch.distributed as dist
 from torch.distributed import distributed_c10d as c10d
 
+from ._library import step_ops
+from .optimizers import Adam
+
 
 def mse(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
-    return torch.mean((pred - target) ** 2)
+    """Keras "mse" of the batch as a device scalar: one kernel forward, one
+    backward (``step_ops.opencl_mse_loss``)."""
+    return step_ops.opencl_mse_loss(pred, target)
 
 
 class GradientAverager:
@@ -129,8 +136,7 @@ class TrainStep:
         self.model = model
         self.params = [p for p in model.parameters() if p.requires_grad]
         dev = self.params[0].device
-        fused = dev.type == "cuda"
-        self.opt = torch.optim.Adam(self.params, lr=lr, fused=fused, capturable=fused)
+        self.opt = Adam(self.params, learning_rate=lr)
         self.avg = GradientAverager(self.params, group)
         self.graphed = graphed and dev.type == "cuda"
         self.warmup = warmup

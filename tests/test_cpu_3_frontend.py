@@ -36,8 +36,9 @@ def test_python_api_names():
 def test_gradient_registry_matches_reference_wiring():
     reference = {"OpenclConv2d", "OpenclDepthwiseConv2d", "OpenclRelu", "OpenclBatchNormTraining", "OpenclSigmoid",
                  "OpenclDense", "OpenclUpsamplingBilinear2d"}
-    # the reference's registrations, plus the fused BatchNorm -> ReLU pair (an extension, not a reference op)
-    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining"}
+    # the reference's registrations, plus the extensions (not reference ops): the fused
+    # BatchNorm -> ReLU pair and the training step's MSE loss
+    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining", "OpenclMseLoss"}
     assert "OpenclBatchNormInference" not in _GRADIENTS
 
 

@@ -79,3 +79,38 @@ def test_netstep_against_float64_autograd(setup, port):
     assert_close(g["stem_w"], P["stem_w"].grad.numpy(), 1e-3, 1e-4, "stem_w")
     assert_close(g["dense_w"], P["dense_w"].grad.numpy(), 1e-3, 1e-4, "dense_w")
     assert_close(g["blocks"][1]["pw"], B[1]["pw"].grad.numpy(), 1e-3, 1e-4, "pw2")
+
+
+def test_keras_adam_restatement_against_float64():
+    """The float32 Keras Adam restatement stays within fp32 rounding of the
+    same formula in float64, over several steps."""
+    from oracle.keras_step import adam_update_f32
+    rng = np.random.default_rng(5)
+    p = rng.standard_normal(1000).astype(np.float32)
+    m = np.zeros_like(p)
+    v = np.zeros_like(p)
+    p64, m64, v64 = p.astype(np.float64), np.zeros(1000), np.zeros(1000)
+    for step in range(5):
+        g = rng.standard_normal(1000).astype(np.float32)
+        p, m, v = adam_update_f32(p, g, m, v, step)
+        t = step + 1
+        alpha = 1e-3 * np.sqrt(1 - 0.999 ** t) / (1 - 0.9 ** t)
+        m64 = m64 + (g - m64) * (1 - 0.9)
+        v64 = v64 + (g.astype(np.float64) ** 2 - v64) * (1 - 0.999)
+        p64 = p64 - m64 * alpha / (np.sqrt(v64) + 1e-7)
+        assert np.abs(m - m64).max() <= 1e-6 * np.abs(m64).max()
+        assert np.abs(v - v64).max() <= 1e-6 * np.abs(v64).max()
+        assert np.abs(p - p64).max() <= 1e-6 * np.abs(p64).max()
+    # the first step moves every parameter by about lr (Adam's normalised step)
+    p0 = rng.standard_normal(100).astype(np.float32)
+    g0 = rng.standard_normal(100).astype(np.float32)
+    p1, _, _ = adam_update_f32(p0, g0, np.zeros(100, np.float32), np.zeros(100, np.float32), 0)
+    assert np.allclose(np.abs(p1 - p0), 1e-3, rtol=1e-3)
+
+
+def test_keras_mse_restatement():
+    from oracle.keras_step import mse_loss_f64, mse_loss_grad_f64
+    p = np.array([[1.0, 2.0], [3.0, 5.0]], np.float32)
+    t = np.array([[0.0, 2.0], [1.0, 1.0]], np.float32)
+    assert mse_loss_f64(p, t) == (1 + 0 + 4 + 16) / 4
+    assert np.array_equal(mse_loss_grad_f64(p, t), 2 * (p - t) / 4)
