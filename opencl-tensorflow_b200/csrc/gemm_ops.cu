@@ -420,7 +420,7 @@ void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_st
 template <int AK, bool kBK>
 int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
                int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
-  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? (int)prob.K : 0);
+  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? im_table_entries(prob.K) : 0);
   static int configured_bytes = 0;  // per instantiation
   if ((int)plan.total > configured_bytes) {
     B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<AK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -455,7 +455,8 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   splits = (int)ceil_div(K, kps);
   const bool use_s = kps > (int64_t)kChunkKB * BK;
   int raw_stages = 0, op_stages = 0;
-  tma_stages(bn, use_s, a.kind == kAFpropRows ? (int)K : 0, d->max_smem_optin, &raw_stages, &op_stages);
+  tma_stages(bn, use_s, a.kind == kAFpropRows ? im_table_entries(K) : 0, d->max_smem_optin, &raw_stages,
+             &op_stages);
   if (raw_stages < 2 || op_stages < 2)
     return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
   TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4};

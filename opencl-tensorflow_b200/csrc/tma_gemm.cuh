@@ -121,8 +121,10 @@ struct TmaSmem {
 };
 
 // Conv2D-forward im2col: staged-row offset of each k = (kh, kw, ci), one int
-// per k, at most this many (K = kH*kW*Ci).
+// per k, at most this many (K = kH*kW*Ci).  The table is padded with zero
+// offsets to a multiple of 32 entries so a k-block reads it four at a time.
 constexpr int kMaxImTable = 1024;
+__host__ __device__ inline int im_table_entries(int64_t K) { return (int)((K + 31) / 32 * 32); }
 
 // Shared memory: a ring of raw stages (TMA destinations: raw A tile + raw B
 // tile), a ring of operand stages (B hi tile + B lo tile, read by the MMA),
@@ -352,8 +354,7 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
 
 // Row r, k = k0 + 16h .. +15 of A, from a landed raw stage.
 template <int AK>
-__device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem& p, const TmaTile& tc, int k0,
-                                           int r, int h, const int* imtab, float (&v)[16]) {
+__device__ __forceinline__ void read_a_row(const uint8_t* raw, int r, int h, float (&v)[16]) {
   if constexpr (AK == kAK) {
     // [128 rows][128 B], 16-byte chunk j of row r at chunk position j ^ (r & 7)
 #pragma unroll
@@ -364,54 +365,108 @@ __device__ __forceinline__ void read_a_row(const uint8_t* raw, const TmaProblem&
       v[4 * j + 2] = q.z;
       v[4 * j + 3] = q.w;
     }
-  } else if constexpr (AK == kAMN) {
+  } else {
     // [4 blocks][32 k][32 rows]
     const float* col = reinterpret_cast<const float*>(raw + (r >> 5) * 4096) + (r & 31);
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = col[(16 * h + i) * 32];
+  }
+}
+
+// Per-tile part of a converter thread's im2col gather (the row kinds): the
+// staged-row offset of its A row, computed once per tile so a k-block costs
+// one offset step per element.
+struct RowGather {
+  int base;  // offset into the staged rows of the row's first element
+};
+
+template <int AK>
+__device__ __forceinline__ RowGather row_gather(const TmaProblem& p, const TmaTile& tc, int r) {
+  const ConvRows& cr = p.cr;
+  RowGather g;
+  if constexpr (AK == kAFpropRows) {
+    // row = output pixel m; its k = (kh, kw, ci) element sits at imtab[k]
+    // from the pixel's base (rows m >= M read in-bounds values and are never
+    // stored)
+    const int m = (int)tc.m0 + r;
+    const int ro = m / cr.Wo, wo = m - ro * cr.Wo;
+    const int j = ro - (int)tc.m0 / cr.Wo;
+    g.base = j * cr.sH * cr.wcp + wo * cr.sW * cr.Ci + (cr.xpad - cr.pW * cr.Ci);
   } else {
-    const ConvRows& cr = p.cr;
-    const float* xs = reinterpret_cast<const float*>(raw);  // [span][wcp], column c at c + xpad
-    const int K = (int)p.K;  // M, K < 2^31 on this path (checked on the host)
-    const int k = k0 + 16 * h;
+    // row = filter element m = (kh, kw, ci); rows m >= M gather element 0's
+    // values (never stored)
+    int m = (int)tc.m0 + r;
+    if (m >= (int)p.M) m = 0;
     const int kwc = cr.kW * cr.Ci;
-    if constexpr (AK == kAFpropRows) {
-      // imtab[k] = kh * wcp + kw * Ci + ci (filled at kernel start)
-      // row = output pixel m; k = (kh, kw, ci) at staged offset kh*wcp + kw*Ci + ci
-      // from the pixel's base (rows m >= M read in-bounds values and are never stored)
-      const int m = (int)tc.m0 + r;
-      const int ro = m / cr.Wo, wo = m - ro * cr.Wo;
-      const int j = ro - (int)tc.m0 / cr.Wo;
-      const float* base = xs + j * cr.sH * cr.wcp + wo * cr.sW * cr.Ci + (cr.xpad - cr.pW * cr.Ci);
+    const int kh = m / kwc, kwci = m - kh * kwc;
+    g.base = kh * cr.wcp + kwci + (cr.xpad - cr.pW * cr.Ci);
+  }
+  return g;
+}
+
+// Both 16-element halves of this thread's A row for the k-block at k0.
+template <int AK>
+__device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem& p, const RowGather& g, int k0,
+                                            const int* imtab, float (&v)[2][16]) {
+  const ConvRows& cr = p.cr;
+  const float* xs = reinterpret_cast<const float*>(raw) + g.base;  // [span][wcp], column c at c + xpad
+  if constexpr (AK == kAFpropRows) {
+    const int K = (int)p.K;  // < 2^31 on this path (checked on the host)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = k + i < K ? base[imtab[k + i]] : 0.0f;
-    } else {
-      // row = filter element m = (kh, kw, ci); k = output pixel (j, wo) at
-      // staged offset j*sH*wcp + wo*sW*Ci from the element's base (K is a
-      // multiple of 32 on this path)
-      const int m = (int)tc.m0 + r;
-      const bool mok = m < (int)p.M;
-      const int kh = m / kwc, kwci = m - kh * kwc;
-      const float* base = xs + kh * cr.wcp + kwci + (cr.xpad - cr.pW * cr.Ci);
-      const int ro = k / cr.Wo;
-      int wo = k - ro * cr.Wo;
-      int b = (ro - k0 / cr.Wo) * cr.sH * cr.wcp + wo * cr.sW * cr.Ci;
-      const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
-      if (cr.Wo >= 16) {
-        // at most one row change in 16 pixels: every offset is independent of
-        // the previous one, so the 16 loads can all be in flight
-        const int n1 = cr.Wo - wo;  // pixels left in the first output row
+    for (int h = 0; h < 2; ++h) {
+      const int k = k0 + 16 * h;
+      const int4* t4 = reinterpret_cast<const int4*>(imtab + k);  // padded table: always in bounds
+      int off[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = mok ? base[b + i * step + (i >= n1 ? wrap - step : 0)] : 0.0f;
+      for (int q = 0; q < 4; ++q) {
+        const int4 o = t4[q];
+        off[4 * q] = o.x;
+        off[4 * q + 1] = o.y;
+        off[4 * q + 2] = o.z;
+        off[4 * q + 3] = o.w;
+      }
+      if (k + 16 <= K) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[h][i] = xs[off[i]];
       } else {
 #pragma unroll
+        for (int i = 0; i < 16; ++i) v[h][i] = k + i < K ? xs[off[i]] : 0.0f;
+      }
+    }
+  } else {
+    // k = output pixel (ro, wo) at staged offset (ro - ro0)*sH*wcp + wo*sW*Ci,
+    // ro0 the k-block's first output row (K is a multiple of 32 on this path)
+    const int ro0 = k0 / cr.Wo;
+    const int wo0 = k0 - ro0 * cr.Wo;
+    const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int wo = wo0 + 16 * h, b = 0;
+      while (wo >= cr.Wo) {  // at most 16 / Wo + 1 times
+        wo -= cr.Wo;
+        b += cr.sH * cr.wcp;
+      }
+      b += wo * step;
+      const int n1 = cr.Wo - wo;  // pixels left in this output row
+      const float* xb = xs + b;
+      if (n1 >= 16) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[h][i] = xb[i * step];
+      } else if (cr.Wo >= 16) {
+        // one row change: every offset is independent of the previous one
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[h][i] = xb[i * step + (i >= n1 ? wrap - step : 0)];
+      } else {
+        int c = 0;
+        wo = cr.Wo - n1;
+#pragma unroll
         for (int i = 0; i < 16; ++i) {
-          v[i] = mok ? base[b] : 0.0f;
+          v[h][i] = xb[c];
           if (++wo == cr.Wo) {
             wo = 0;
-            b += wrap;
+            c += wrap;
           } else {
-            b += step;
+            c += step;
           }
         }
       }
@@ -438,7 +493,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
-  const int table_entries = AK == kAFpropRows ? (int)p.K : 0;
+  const int table_entries = AK == kAFpropRows ? im_table_entries(p.K) : 0;
   const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages, table_entries);
   int* imtab = reinterpret_cast<int*>(smem + plan.table_offset);
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + plan.bar_offset);
@@ -499,7 +554,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   if constexpr (AK == kAFpropRows) {
     const int kwc = p.cr.kW * p.cr.Ci;
-    for (int k = threadIdx.x; k < table_entries; k += blockDim.x) imtab[k] = (k / kwc) * p.cr.wcp + k % kwc;
+    for (int k = threadIdx.x; k < table_entries; k += blockDim.x)
+      imtab[k] = k < (int)p.K ? (k / kwc) * p.cr.wcp + k % kwc : 0;
   }
   if (warp == kTmaMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -546,6 +602,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       const TmaTile tc = tma_tile(p, t);
+      RowGather rg{};
+      if constexpr (AK == kAFpropRows || AK == kAWgradRows) rg = row_gather<AK>(p, tc, row);
       for (int kb = 0; kb < tc.nkb; ++kb, ++i) {
         if ((int)(i & 1u) != group) continue;
         const uint32_t sr = i % R, sq = i % Q;
@@ -556,8 +614,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const uint8_t* raw = smem + (size_t)sr * plan.raw_bytes;
         float va[2][16];
         const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
-        read_a_row<AK>(raw, p, tc, k0, row, 0, imtab, va[0]);
-        read_a_row<AK>(raw, p, tc, k0, row, 1, imtab, va[1]);
+        if constexpr (AK == kAFpropRows || AK == kAWgradRows) {
+          read_a_rows<AK>(raw, p, rg, k0, imtab, va);
+        } else {
+          read_a_row<AK>(raw, row, 0, va[0]);
+          read_a_row<AK>(raw, row, 1, va[1]);
+        }
         uint4 wb[kMaxBWords];
 #pragma unroll
         for (int j = 0; j < kMaxBWords; ++j)
