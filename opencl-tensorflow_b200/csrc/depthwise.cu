@@ -3,20 +3,29 @@
 // Reference: kernels/depthwise_conv2d_kernels.cl, src/ops/
 // depthwise_conv2d_ops.cc.  Output channel co = ci*dm + d sees only input
 // channel ci.  These ops are HBM-bound (about 2*kH*kW flops per output), so
-// the kernels are built around coalesced NHWC traffic:
+// the kernels are built around coalesced NHWC traffic.  Taps are always
+// summed in the reference's (kh, kw[, d]) order with round-to-nearest
+// multiply and add, so forward and input gradient are bit-identical to the
+// reference's sequential fp32 sums.
 //
-//   forward / input gradient, dm == 1 and C % 4 == 0: one thread per
-//     (pixel, 4 channels) with 128-bit loads; taps summed in the reference's
-//     (kh, kw[, d]) order with round-to-nearest multiply and add, so every
-//     output is bit-identical to the reference's sequential fp32 sum;
-//   other shapes: one thread per element, same order, same exactness;
-//   input gradient, dm == 1 and C % 4 == 0: one CTA per input row (decoded
-//     once), threads over (pixel of the row, 4 channels), same order;
-//   filter gradient: a sum over N*Ho*Wo per filter element, done as per-CTA
-//     partial sums (each thread owns 4 channels x all taps, CTAs fold their
-//     pixel lanes in a fixed order) plus a finalize that adds the partials in
-//     a fixed tree, so it is deterministic; with dm > 1 or C % 4 != 0 a
-//     scalar variant of the same two stages.
+//   forward, 3x3 stride 2, dm == 1, C % 4 == 0 (the README blocks):
+//     dw_fwd_s2k3_kernel -- a thread computes two horizontally adjacent
+//     outputs for 4 channels, loading the five input columns they share once,
+//     with the filter held in registers;
+//   forward, other dm == 1 / C % 4 == 0 shapes: one thread per (pixel, 4
+//     channels) with 128-bit loads (dw_fwd_vec4_kernel); any other shape: one
+//     thread per element (dw_fwd_scalar_kernel);
+//   input gradient, 3x3 stride 2: dw_dgrad_s2k3_kernel -- column pairs that
+//     share each dy load, filter in registers; other dm == 1 shapes: one CTA
+//     per input row (dw_dgrad_rows_kernel); any shape: dw_dgrad_scalar_kernel;
+//   filter gradient (a sum over N*Ho*Wo per filter element), deterministic in
+//     two stages: per-CTA partials, then dw_wgrad_finalize_kernel adding them
+//     in a fixed tree.  For dm == 1, C % 4 == 0 the partials come from
+//     dw_wgrad_staged_kernel: a producer warp streams dy rows and zero-padded
+//     input rows into a ring of shared-memory slots with 1-D bulk copies
+//     (full / empty mbarriers, every wait bounded), consumer warps accumulate
+//     all taps from shared memory; otherwise from the register-walking
+//     dw_wgrad_partial_vec4_kernel / _scalar_kernel.
 #include "conv_common.cuh"
 
 namespace b2 {
