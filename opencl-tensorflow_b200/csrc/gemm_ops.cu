@@ -407,10 +407,11 @@ int tma_bn(int64_t N) {
 
 // Operand stages: limited by the TMEM columns left for A slots; raw stages
 // take the remaining shared memory.
-void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_stages, int* op_stages) {
+void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_stages, int* op_stages,
+                int b_res_kb = 0) {
   int q = (int)((kTmemCols - tma_acc_cols(bn, use_s)) / kASlotCols);
   if (q > kTmaMaxOpStages) q = kTmaMaxOpStages;
-  const TmaSmem fixed = tma_smem_plan(bn, 0, q, table_entries);
+  const TmaSmem fixed = tma_smem_plan(bn, 0, q, table_entries, b_res_kb);
   int r = (int)((max_smem - (int)fixed.total) / (int)fixed.raw_bytes);
   if (r > kTmaMaxStages) r = kTmaMaxStages;
   *raw_stages = r;
@@ -420,7 +421,8 @@ void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_st
 template <int AK, bool kBK>
 int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const TmaProblem& prob,
                int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
-  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? im_table_entries(prob.K) : 0);
+  const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? im_table_entries(prob.K) : 0,
+                                     prob.b_res_kb);
   static int configured_bytes = 0;  // per instantiation
   if ((int)plan.total > configured_bytes) {
     B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<AK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -454,12 +456,29 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   if (kps < BK) kps = BK;
   splits = (int)ceil_div(K, kps);
   const bool use_s = kps > (int64_t)kChunkKB * BK;
+  const int table = a.kind == kAFpropRows ? im_table_entries(K) : 0;
   int raw_stages = 0, op_stages = 0;
-  tma_stages(bn, use_s, a.kind == kAFpropRows ? im_table_entries(K) : 0, d->max_smem_optin, &raw_stages,
-             &op_stages);
+  // Resident B: with one split and a short K, every tile of a CTA multiplies
+  // by the same B tile when the grid is a multiple of the N-tile count; it is
+  // then loaded and split once per CTA instead of once per k-block.
+  const int64_t nt = ceil_div(N, bn);
+  int b_res_kb = 0;
+  int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
+  if (splits == 1 && K <= (int64_t)kTmaMaxResKB * BK && grid / nt * nt > 0 &&
+      ceil_div(K, BK) * 2 * (int64_t)bn * BK * 4 <= kTmaMaxResBytes) {
+    tma_stages(bn, use_s, table, d->max_smem_optin, &raw_stages, &op_stages, (int)ceil_div(K, BK));
+    if (raw_stages >= 3) {
+      b_res_kb = (int)ceil_div(K, BK);
+      grid = (int)(grid / nt * nt);
+    }
+  }
+  if (b_res_kb == 0) tma_stages(bn, use_s, table, d->max_smem_optin, &raw_stages, &op_stages);
   if (raw_stages < 2 || op_stages < 2)
     return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
-  TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4};
+  TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4, b_res_kb};
+  B2_REQUIRE(tiles * splits <= kMaxInt32, "%s: too many output tiles", name);
+  prob.nt_div = FastDiv((uint32_t)nt);
+  prob.mt_div = FastDiv((uint32_t)ceil_div(M, BM));
   CUtensorMap ma, mb, md;
   if (a.kind == kAK || a.kind == kAMN) {
     B2_RETURN_IF_ERROR(encode_operand(&ma, a.mat, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));
@@ -487,7 +506,6 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
     prob.partial = true;
     prob.bias = nullptr;
   }
-  const int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
   int rc;
   switch (a.kind) {
     case kAK:

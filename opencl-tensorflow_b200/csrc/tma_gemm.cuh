@@ -75,6 +75,8 @@ constexpr int kTmaThreads = 32 * (kTmaEpiWarp0 + 4);
 constexpr int kTmaMaxStages = 8;    // raw (TMA) stages
 constexpr int kTmaMaxOpStages = 4;  // operand stages (B hi/lo in smem + A hi/lo in TMEM)
 constexpr int kTmaMaxBN = 96;
+constexpr int kTmaMaxResKB = 5;                 // resident B: at most this many k-blocks (K <= 160)
+constexpr int64_t kTmaMaxResBytes = 120 << 10;  // and at most this much shared memory
 constexpr uint32_t kEpiBuf = 32 * 128;  // one 32 x 32 fp32 output block
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kASlotCols = 2 * BK;  // A hi and lo of one k-block
@@ -100,6 +102,23 @@ struct ConvRows {
   int wcp;   // staged row width (floats, multiple of 4, <= 256)
 };
 
+// Division by a divisor fixed at launch, for 32-bit dividends: q = (hi32(n *
+// mul) + n) >> shift with mul, shift chosen on the host (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", PLDI
+// 1994) -- a multiply-high, an add and a shift instead of a division routine
+// on the per-tile critical path of every warp role.
+struct FastDiv {
+  uint32_t d, mul, shift;
+  __host__ __device__ FastDiv() : d(1), mul(1), shift(0) {}
+  __host__ explicit FastDiv(uint32_t div) : d(div), mul(1), shift(0) {
+    while ((1ull << shift) < div) ++shift;
+    mul = (uint32_t)(((1ull << 32) * ((1ull << shift) - div)) / div + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return (uint32_t)(((uint64_t)__umulhi(n, mul) + n) >> shift);
+  }
+};
+
 struct TmaProblem {
   ConvRows cr;
   int64_t M, N, K;
@@ -110,6 +129,9 @@ struct TmaProblem {
   bool partial;       // out is [splits][M][N] partials (3-D store map)
   bool use_s;         // some tile spans several chunks: keep a running sum S
   uint32_t a_tx;      // bytes of the raw A load per k-block (<= 16 KB)
+  int b_res_kb;       // > 0: every tile of a CTA shares one B tile of this many
+                      // k-blocks, loaded and split once and kept in shared memory
+  FastDiv nt_div, mt_div;  // N tiles, M tiles (tile indices < 2^31)
 };
 
 // TMEM columns used by the accumulators (P0, P1 and, when needed, S).
@@ -128,19 +150,22 @@ __host__ __device__ inline int im_table_entries(int64_t K) { return (int)((K + 3
 
 // Shared memory: a ring of raw stages (TMA destinations: raw A tile + raw B
 // tile), a ring of operand stages (B hi tile + B lo tile, read by the MMA),
-// the epilogue buffers and the barriers.
-__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_stages, int table_entries) {
+// the epilogue buffers and the barriers.  With a resident B (b_res_kb > 0)
+// the raw stages hold A only and the operand area holds B hi / lo of every
+// k-block of the CTA's B tile, indexed by k-block.
+__host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_stages, int table_entries,
+                                                 int b_res_kb = 0) {
   TmaSmem s;
   s.raw_stages = raw_stages;
   s.op_stages = op_stages;
   s.a_bytes = (uint32_t)BM * BK * 4;
   s.b_bytes = (uint32_t)bn * BK * 4;
-  s.raw_bytes = s.a_bytes + s.b_bytes;
+  s.raw_bytes = s.a_bytes + (b_res_kb > 0 ? 0u : s.b_bytes);
   s.op_bytes = 2 * s.b_bytes;
   s.op_offset = s.raw_bytes * (uint32_t)raw_stages;
-  s.epi_offset = s.op_offset + s.op_bytes * (uint32_t)op_stages;
+  s.epi_offset = s.op_offset + s.op_bytes * (uint32_t)(b_res_kb > 0 ? b_res_kb : op_stages);
   s.bar_offset = s.epi_offset + 4 * (uint32_t)(bn / 32) * kEpiBuf;  // a 32 x BN block per epilogue warp
-  s.table_offset = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4) + 16;
+  s.table_offset = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4 + 2) + 16;
   s.total = s.table_offset + 4 * (uint32_t)table_entries + 1024;  // + alignment slack
   return s;
 }
@@ -304,13 +329,14 @@ struct TmaTile {
 };
 
 __device__ __forceinline__ TmaTile tma_tile(const TmaProblem& p, int64_t t) {
-  const int64_t nt = (p.N + p.bn - 1) / p.bn, mt = (p.M + BM - 1) / BM;
   TmaTile c;
-  const int64_t n_idx = t % nt;
-  const int64_t rest = t / nt;
-  c.m0 = (rest % mt) * BM;
-  c.z = (int)(rest / mt);
-  c.n0 = n_idx * p.bn;
+  const uint32_t t32 = (uint32_t)t;
+  const uint32_t rest = p.nt_div.div(t32);
+  const uint32_t n_idx = t32 - rest * p.nt_div.d;
+  const uint32_t z = p.mt_div.div(rest);
+  c.m0 = (int64_t)(rest - z * p.mt_div.d) * BM;
+  c.z = (int)z;
+  c.n0 = (int64_t)n_idx * p.bn;
   c.k_begin = (int64_t)c.z * p.k_per_split;
   c.k_end = c.k_begin + p.k_per_split;
   if (c.k_end > p.K) c.k_end = p.K;
@@ -329,6 +355,16 @@ __device__ __forceinline__ void staged_rows(const ConvRows& cr, int64_t p0, int*
 // Loads of one k-block (raw A: tile or staged input rows; raw B tile
 // BN x 32) into a raw stage.
 template <int AK, bool kBK>
+__device__ __forceinline__ void issue_b(const CUtensorMap* map_b, uint32_t dst, uint64_t* bar, int bn, int64_t n0,
+                                        int k0) {
+  if constexpr (kBK) {
+    tma_load_2d(dst, map_b, k0, (int)n0, bar);
+  } else {
+    for (int b = 0; b < bn / 32; ++b) tma_load_2d(dst + 4096u * b, map_b, (int)n0 + 32 * b, k0, bar);
+  }
+}
+
+template <int AK, bool kBK>
 __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUtensorMap* map_b, uint32_t st,
                                             uint32_t a_bytes, uint64_t* bar, uint32_t tx, const TmaProblem& p,
                                             const TmaTile& tc, int kb) {
@@ -345,11 +381,7 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
     staged_rows(p.cr, AK == kAFpropRows ? tc.m0 : (int64_t)k0, &n, &hi_first);
     tma_load_3d(st, map_a, -p.cr.xpad, hi_first, n, bar);
   }
-  if constexpr (kBK) {
-    tma_load_2d(b_raw, map_b, k0, (int)tc.n0, bar);
-  } else {
-    for (int b = 0; b < p.bn / 32; ++b) tma_load_2d(b_raw + 4096u * b, map_b, (int)tc.n0 + 32 * b, k0, bar);
-  }
+  if (p.b_res_kb == 0) issue_b<AK, kBK>(map_b, b_raw, bar, p.bn, tc.n0, k0);
 }
 
 // Row r, k = k0 + 16h .. +15 of A, from a landed raw stage.
@@ -494,7 +526,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
   const int table_entries = AK == kAFpropRows ? im_table_entries(p.K) : 0;
-  const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages, table_entries);
+  const bool bres = p.b_res_kb > 0;
+  const TmaSmem plan = tma_smem_plan(bn, raw_stages, op_stages, table_entries, p.b_res_kb);
   int* imtab = reinterpret_cast<int*>(smem + plan.table_offset);
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + plan.bar_offset);
   uint64_t* raw_empty = raw_full + kTmaMaxStages;
@@ -502,7 +535,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint64_t* op_empty = op_full + kTmaMaxOpStages;
   uint64_t* chunk_full = op_empty + kTmaMaxOpStages;  // [2]
   uint64_t* chunk_empty = chunk_full + 2;             // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
+  uint64_t* b_full = chunk_empty + 2;                 // resident B landed
+  uint64_t* b_ready = b_full + 1;                     // resident B split (one arrival per converter warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_ready + 1);
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
 
@@ -512,7 +547,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int64_t tiles = nt * mt * p.splits;
   const uint32_t acc_cols = (uint32_t)bn;
   const uint32_t a_col0 = tma_acc_cols(bn, p.use_s);  // first A slot column
-  const uint32_t tx = p.a_tx + plan.b_bytes;  // bytes the TMA delivers per k-block
+  const uint32_t tx = p.a_tx + (bres ? 0u : plan.b_bytes);  // bytes the TMA delivers per k-block
   const uint32_t R = (uint32_t)raw_stages, Q = (uint32_t)op_stages;
 
   // TMA issue cursor (lane 0 of warp 0): tile t, k-block kb, raw stage use it.
@@ -534,10 +569,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       mbar_init(&chunk_full[a], 1);
       mbar_init(&chunk_empty[a], 128);
     }
+    mbar_init(b_full, 1);
+    mbar_init(b_ready, kConvWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&map_a);
     prefetch_map(&map_b);
     prefetch_map(&map_d);
+    if (bres && blockIdx.x < tiles) {
+      // every tile of this CTA has n-tile blockIdx.x % nt (the grid is a multiple of nt)
+      mbar_expect_tx(b_full, (uint32_t)p.b_res_kb * plan.b_bytes);
+      for (int kb = 0; kb < p.b_res_kb; ++kb)
+        issue_b<AK, kBK>(&map_b, smem_u32(smem + plan.op_offset + (size_t)kb * plan.op_bytes), b_full, bn,
+                         (blockIdx.x % nt) * bn, kb * BK);
+    }
     // The first round of raw stages needs no EMPTY wait: issue it before the
     // block-wide barrier so the loads overlap the TMEM allocation.
     if (t_iss < tiles) tc_iss = tma_tile(p, t_iss);
@@ -571,12 +615,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   if (warp == kTmaWarp) {
     // ---------------------------------------------------------- TMA issue
     if (lane == 0) {
+      uint32_t s = 0, lap = 1;  // it_iss = lap * R + s (it_iss == R here unless the work ran out)
       while (t_iss < tiles) {
-        const uint32_t s = it_iss % R;
-        if (!mbar_wait(&raw_empty[s], (it_iss / R - 1) & 1u, abort_flag)) break;
+        if (!mbar_wait(&raw_empty[s], (lap - 1) & 1u, abort_flag)) break;
         issue_stage<AK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.raw_bytes), plan.a_bytes,
                              &raw_full[s], tx, p, tc_iss, kb_iss);
         ++it_iss;
+        if (++s == R) {
+          s = 0;
+          ++lap;
+        }
         if (++kb_iss == tc_iss.nkb) {
           kb_iss = 0;
           t_iss += gridDim.x;
@@ -586,6 +634,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       // Let every issued load land before the CTA can exit.
       const uint32_t n = it_iss < R ? it_iss : R;
       for (uint32_t i = it_iss - n; i < it_iss; ++i) mbar_wait_drain(&raw_full[i % R], (i / R) & 1u);
+      if (bres && blockIdx.x < tiles) mbar_wait_drain(b_full, 0);
     }
   } else if (warp >= kConvWarp0 && warp < kTmaEpiWarp0) {
     // ---------------------------------------------------------- converters
@@ -599,15 +648,44 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const uint32_t a_taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + a_col0;
     const int b_words = bn * BK * 4 / 16;
     uint32_t i = 0;  // k-block sequence number
+    uint32_t sr = 0, lap_r = 0, sq = 0, lap_q = 0;  // i = lap_r * R + sr = lap_q * Q + sq
     bool ok = true;
+    if (bres && blockIdx.x < tiles) {
+      // split the resident B tile in place, all converter warps together
+      ok = mbar_wait(b_full, 0, abort_flag);
+      if (ok) {
+        const int ct = (warp - kConvWarp0) * 32 + lane;
+        const int words = p.b_res_kb * b_words;
+        for (int w = ct; w < words; w += kConvWarps * 32) {
+          const int kbw = w / b_words, wi = w - kbw * b_words;
+          uint8_t* hi = smem + plan.op_offset + (size_t)kbw * plan.op_bytes + 16 * wi;
+          uint4 h, l;
+          split_word(*reinterpret_cast<const uint4*>(hi), h, l);
+          *reinterpret_cast<uint4*>(hi) = h;
+          *reinterpret_cast<uint4*>(hi + plan.b_bytes) = l;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_ready);
+    }
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
       const TmaTile tc = tma_tile(p, t);
       RowGather rg{};
       if constexpr (AK == kAFpropRows || AK == kAWgradRows) rg = row_gather<AK>(p, tc, row);
       for (int kb = 0; kb < tc.nkb; ++kb, ++i) {
+        const uint32_t cur_sr = sr, cur_lr = lap_r, cur_sq = sq, cur_lq = lap_q;
+        if (++sr == R) {
+          sr = 0;
+          ++lap_r;
+        }
+        if (++sq == Q) {
+          sq = 0;
+          ++lap_q;
+        }
         if ((int)(i & 1u) != group) continue;
-        const uint32_t sr = i % R, sq = i % Q;
-        if (!mbar_wait(&raw_full[sr], (i / R) & 1u, abort_flag)) {
+        const uint32_t sr = cur_sr, sq = cur_sq;
+        if (!mbar_wait(&raw_full[sr], cur_lr & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -623,11 +701,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         uint4 wb[kMaxBWords];
 #pragma unroll
         for (int j = 0; j < kMaxBWords; ++j)
-          if (gt + j * kGroupThreads < b_words)
+          if (!bres && gt + j * kGroupThreads < b_words)
             wb[j] = *reinterpret_cast<const uint4*>(raw + plan.a_bytes + 16 * (gt + j * kGroupThreads));
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[sr]);  // this warp has read the raw stage
-        if (i >= Q && !mbar_wait(&op_empty[sq], (i / Q - 1) & 1u, abort_flag)) {
+        if (cur_lq > 0 && !mbar_wait(&op_empty[sq], (cur_lq - 1) & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -643,7 +721,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         uint8_t* bh = smem + plan.op_offset + (size_t)sq * plan.op_bytes;
 #pragma unroll
         for (int j = 0; j < kMaxBWords; ++j)
-          if (gt + j * kGroupThreads < b_words) {
+          if (!bres && gt + j * kGroupThreads < b_words) {
             uint4 h, l;
             split_word(wb[j], h, l);
             *reinterpret_cast<uint4*>(bh + 16 * (gt + j * kGroupThreads)) = h;
@@ -661,7 +739,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32_major(bn, false, !kBK);
       uint32_t it = 0, g = 0;  // g counts chunks
-      bool ok = true;
+      uint32_t sq = 0, lap_q = 0;  // it = lap_q * Q + sq
+      bool ok = !(bres && blockIdx.x < tiles) || mbar_wait(b_ready, 0, abort_flag);
       for (int64_t t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
         const TmaTile tc = tma_tile(p, t);
         for (int kb0 = 0; kb0 < tc.nkb && ok; kb0 += kChunkKB, ++g) {
@@ -675,14 +754,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
           const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            const uint32_t sq = it % Q;
-            if (!mbar_wait(&op_full[sq], (it / Q) & 1u, abort_flag)) {
+            if (!mbar_wait(&op_full[sq], lap_q & 1u, abort_flag)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a_hi = tmem_base + a_col0 + sq * kASlotCols, a_lo = a_hi + BK;
-            const uint32_t b_hi = smem_u32(smem + plan.op_offset + (size_t)sq * plan.op_bytes);
+            const uint32_t b_hi = smem_u32(smem + plan.op_offset + (size_t)(bres ? (uint32_t)kb : sq) * plan.op_bytes);
             const uint32_t b_lo = b_hi + plan.b_bytes;
 #pragma unroll
             for (int j = 0; j < BK / 8; ++j) {
@@ -691,6 +769,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_hi, j), idesc, 1u);
             }
             mma_commit(&op_empty[sq]);
+            if (++sq == Q) {
+              sq = 0;
+              ++lap_q;
+            }
           }
           mma_commit(&chunk_full[a]);
         }
