@@ -479,6 +479,11 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   B2_REQUIRE(tiles * splits <= kMaxInt32, "%s: too many output tiles", name);
   prob.nt_div = FastDiv((uint32_t)nt);
   prob.mt_div = FastDiv((uint32_t)ceil_div(M, BM));
+  if (a.kind == kAFpropRows || a.kind == kAWgradRows) {
+    prob.wo_div = FastDiv((uint32_t)a.cr.Wo);
+    prob.ho_div = FastDiv((uint32_t)a.cr.Ho);
+    prob.kwc_div = FastDiv((uint32_t)(a.cr.kW * a.cr.Ci));
+  }
   CUtensorMap ma, mb, md;
   if (a.kind == kAK || a.kind == kAMN) {
     B2_RETURN_IF_ERROR(encode_operand(&ma, a.mat, K, BM, CU_TENSOR_MAP_SWIZZLE_NONE));

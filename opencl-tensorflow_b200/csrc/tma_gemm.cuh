@@ -132,6 +132,7 @@ struct TmaProblem {
   int b_res_kb;       // > 0: every tile of a CTA shares one B tile of this many
                       // k-blocks, loaded and split once and kept in shared memory
   FastDiv nt_div, mt_div;  // N tiles, M tiles (tile indices < 2^31)
+  FastDiv wo_div, ho_div, kwc_div;  // conv kinds: Wo, Ho and kW * Ci
 };
 
 // TMEM columns used by the accumulators (P0, P1 and, when needed, S).
@@ -346,9 +347,10 @@ __device__ __forceinline__ TmaTile tma_tile(const TmaProblem& p, int64_t t) {
 
 // First output row (n * Ho + ho) of the pixels [p0, ...) and the input row
 // its staging starts at.
-__device__ __forceinline__ void staged_rows(const ConvRows& cr, int64_t p0, int* n, int* hi_first) {
-  const int ro = (int)(p0 / cr.Wo);
-  *n = ro / cr.Ho;
+__device__ __forceinline__ void staged_rows(const TmaProblem& p, int64_t p0, int* n, int* hi_first) {
+  const ConvRows& cr = p.cr;
+  const int ro = (int)p.wo_div.div((uint32_t)p0);  // pixel indices < 2^31 on these paths
+  *n = (int)p.ho_div.div((uint32_t)ro);
   *hi_first = (ro - *n * cr.Ho) * cr.sH - cr.pH;
 }
 
@@ -378,7 +380,7 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* map_a, const CUte
     for (int b = 0; b < BM / 32; ++b) tma_load_2d(st + 4096u * b, map_a, (int)tc.m0 + 32 * b, k0, bar);
   } else {
     int n, hi_first;
-    staged_rows(p.cr, AK == kAFpropRows ? tc.m0 : (int64_t)k0, &n, &hi_first);
+    staged_rows(p, AK == kAFpropRows ? tc.m0 : (int64_t)k0, &n, &hi_first);
     tma_load_3d(st, map_a, -p.cr.xpad, hi_first, n, bar);
   }
   if (p.b_res_kb == 0) issue_b<AK, kBK>(map_b, b_raw, bar, p.bn, tc.n0, k0);
@@ -421,8 +423,8 @@ __device__ __forceinline__ RowGather row_gather(const TmaProblem& p, const TmaTi
     // from the pixel's base (rows m >= M read in-bounds values and are never
     // stored)
     const int m = (int)tc.m0 + r;
-    const int ro = m / cr.Wo, wo = m - ro * cr.Wo;
-    const int j = ro - (int)tc.m0 / cr.Wo;
+    const int ro = (int)p.wo_div.div((uint32_t)m), wo = m - ro * cr.Wo;
+    const int j = ro - (int)p.wo_div.div((uint32_t)tc.m0);
     g.base = j * cr.sH * cr.wcp + wo * cr.sW * cr.Ci + (cr.xpad - cr.pW * cr.Ci);
   } else {
     // row = filter element m = (kh, kw, ci); rows m >= M gather element 0's
@@ -430,7 +432,7 @@ __device__ __forceinline__ RowGather row_gather(const TmaProblem& p, const TmaTi
     int m = (int)tc.m0 + r;
     if (m >= (int)p.M) m = 0;
     const int kwc = cr.kW * cr.Ci;
-    const int kh = m / kwc, kwci = m - kh * kwc;
+    const int kh = (int)p.kwc_div.div((uint32_t)m), kwci = m - kh * kwc;
     g.base = kh * cr.wcp + kwci + (cr.xpad - cr.pW * cr.Ci);
   }
   return g;
@@ -468,7 +470,7 @@ __device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem
   } else {
     // k = output pixel (ro, wo) at staged offset (ro - ro0)*sH*wcp + wo*sW*Ci,
     // ro0 the k-block's first output row (K is a multiple of 32 on this path)
-    const int ro0 = k0 / cr.Wo;
+    const int ro0 = (int)p.wo_div.div((uint32_t)k0);
     const int wo0 = k0 - ro0 * cr.Wo;
     const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
 #pragma unroll
