@@ -207,36 +207,42 @@ __global__ void __launch_bounds__(kThreads)
       a += s_a[r * width + i];
       b += s_b[r * width + i];
     }
-    partial[(int64_t)blockIdx.x * C + c] = make_float2(a, b);
+    partial[(int64_t)c * gridDim.x + blockIdx.x] = make_float2(a, b);  // channel-major: [C][blocks]
   }
 }
 
 // Stage 2 for the statistics: saved_mean, saved_var (biased, E[x^2]-mean^2 as
 // batchnorm_kernels.cl:57-59) and the constants of the normalize pass.
-// Sum of the partials of channel c over all row blocks, in a fixed order:
-// thread t adds blocks t, t + kFinThreads, ... in order, then the CTA adds the
-// thread sums in a fixed pairwise tree.  One CTA of kFinThreads per channel.
+// Sum of the partials of channel c over all row blocks, in a fixed order: the
+// partials are stored channel-major, thread t adds blocks t, t + kFinThreads,
+// ... in order (coalesced across the CTA), each warp folds its 32 sums with a
+// fixed xor butterfly, and thread 0 adds the warp sums in warp order.  One
+// CTA of kFinThreads per channel.
 constexpr int kFinThreads = 128;
 __device__ __forceinline__ float2 sum_partials(const float2* __restrict__ partial, int blocks, int C, int c) {
-  __shared__ float2 s_red[kFinThreads];
+  __shared__ float2 s_warp[kFinThreads / 32];
+  const float2* pc = partial + (int64_t)c * blocks;
   float a = 0.0f, b = 0.0f;
 #pragma unroll 4
   for (int i = threadIdx.x; i < blocks; i += kFinThreads) {
-    const float2 p = partial[(int64_t)i * C + c];
+    const float2 p = pc[i];
     a += p.x;
     b += p.y;
   }
-  s_red[threadIdx.x] = make_float2(a, b);
-  __syncthreads();
-  for (int h = kFinThreads / 2; h > 0; h >>= 1) {
-    if ((int)threadIdx.x < h) {
-      const float2 o = s_red[threadIdx.x + h];
-      s_red[threadIdx.x].x += o.x;
-      s_red[threadIdx.x].y += o.y;
-    }
-    __syncthreads();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
   }
-  return s_red[0];
+  if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = make_float2(a, b);
+  __syncthreads();
+  float2 r = s_warp[0];
+#pragma unroll
+  for (int w = 1; w < kFinThreads / 32; ++w) {
+    r.x += s_warp[w].x;
+    r.y += s_warp[w].y;
+  }
+  return r;
 }
 
 // Stage 2 of the statistics: mean = sum / NHW, var = sum_sq / NHW - mean^2

@@ -104,19 +104,12 @@ __global__ void __launch_bounds__(kThreads) dw_fwd_vec4_kernel(const float* __re
 __global__ void __launch_bounds__(kThreads) dw_fwd_s2k3_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ w, float* __restrict__ y,
                                                                 DwArgs a, int pairs, int rows_per_block) {
-  // the CTA's filter taps in shared memory, [9][blockDim.x] float4: registers
-  // go to the input columns in flight instead
-  extern __shared__ float4 sw[];
-  const int C4 = a.C >> 2;
-  for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 9 * (int)blockDim.x; i += blockDim.x * blockDim.y) {
-    const int k = i / blockDim.x, cl = i - k * blockDim.x, cg = blockIdx.y * blockDim.x + cl;
-    if (cg < C4) sw[i] = __ldg(reinterpret_cast<const float4*>(w) + k * C4 + cg);
-  }
-  __syncthreads();
   const int c4 = blockIdx.y * blockDim.x + threadIdx.x;
-  if (c4 >= C4) return;
-  const float4* wt = sw + threadIdx.x;  // tap k at wt[k * blockDim.x]
+  if (c4 >= (a.C >> 2)) return;
   const int C = a.C, c = 4 * c4;
+  float4 wr[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) wr[k] = __ldg(reinterpret_cast<const float4*>(w + k * C + c));
   const int rows = a.N * a.Ho;
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
@@ -128,25 +121,27 @@ __global__ void __launch_bounds__(kThreads) dw_fwd_s2k3_kernel(const float* __re
     float* yrow = y + (int64_t)r * a.Wo * C + c;
     for (int j = threadIdx.y; j < pairs; j += blockDim.y) {
       const int wi0 = 4 * j - a.pW;  // first input column of output 2j
-      bool okc[5];
+      float4 v[3][5];
+      bool okr[3], okc[5];
 #pragma unroll
       for (int q = 0; q < 5; ++q) okc[q] = (unsigned)(wi0 + q) < (unsigned)a.W;
-      float4 a0 = z, a1 = z;
-      // input rows one at a time, taps in the reference's (kh, kw) order
 #pragma unroll
       for (int kh = 0; kh < 3; ++kh) {
         const int hi = hi0 + kh;
-        if ((unsigned)hi >= (unsigned)a.H) continue;
+        okr[kh] = (unsigned)hi < (unsigned)a.H;
         const float* xr = ximg + (int64_t)hi * a.W * C;
-        float4 v[5];
 #pragma unroll
         for (int q = 0; q < 5; ++q)
-          v[q] = okc[q] ? __ldg(reinterpret_cast<const float4*>(xr + (int64_t)(wi0 + q) * C)) : z;
+          v[kh][q] = okr[kh] && okc[q] ? __ldg(reinterpret_cast<const float4*>(xr + (int64_t)(wi0 + q) * C)) : z;
+      }
+      float4 a0 = z, a1 = z;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+        if (!okr[kh]) continue;
 #pragma unroll
         for (int kw = 0; kw < 3; ++kw) {
-          const float4 wk = wt[(kh * 3 + kw) * blockDim.x];
-          if (okc[kw]) a0 = fadd4(a0, fmul4(v[kw], wk));
-          if (okc[kw + 2]) a1 = fadd4(a1, fmul4(v[kw + 2], wk));
+          if (okc[kw]) a0 = fadd4(a0, fmul4(v[kh][kw], wr[kh * 3 + kw]));
+          if (okc[kw + 2]) a1 = fadd4(a1, fmul4(v[kh][kw + 2], wr[kh * 3 + kw]));
         }
       }
       const int wo0 = 2 * j;
@@ -767,7 +762,7 @@ int b2_depthwise_conv2d(b2_stream_t stream, const float* input, const int64_t in
       int64_t rpb = ceil_div(rows, want);
       if (rpb > 8) rpb = 8;
       const dim3 grid((unsigned)ceil_div(rows, rpb), (unsigned)chunks);
-      dw_fwd_s2k3_kernel<<<grid, blk, 9 * blk.x * sizeof(float4), s>>>(input, filter, output, a, pairs, (int)rpb);
+      dw_fwd_s2k3_kernel<<<grid, blk, 0, s>>>(input, filter, output, a, pairs, (int)rpb);
     } else {
       dw_fwd_vec4_kernel<<<grid_for(g.out_elems() / 4, kThreads, 8), kThreads, 0, s>>>(input, filter, output, a);
     }
