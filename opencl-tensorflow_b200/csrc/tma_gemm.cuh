@@ -243,14 +243,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 3xTF32 operand split: x = hi + lo with hi = tf32(x) rounded to nearest
-// (ties away from zero: add half a tf32 ulp to the magnitude, clear the 13
-// dropped bits; Inf and NaN pass through) and lo = x - hi, exact in fp32.
-// The tensor core reads the top 19 bits of each element, so lo enters
-// truncated to tf32; since lo has either sign that error is unbiased, and
-// hi + lo carries x to within 2^-21 |x| (typically ~2^-23).
+// 3xTF32 operand split: x = hi + lo with hi = tf32(x) rounded to nearest,
+// ties away from zero (one `cvt.rna.tf32.f32`, the same bits as adding half a
+// tf32 ulp to the magnitude and clearing the 13 dropped bits; Inf stays Inf,
+// NaN stays NaN) and lo = x - hi, exact in fp32.  The tensor core reads the
+// top 19 bits of each element, so lo enters truncated to tf32; since lo has
+// either sign that error is unbiased, and hi + lo carries x to within
+// 2^-21 |x| (typically ~2^-23).
 __device__ __forceinline__ uint32_t tf32_hi_bits(uint32_t u) {
-  return (u & 0x7F800000u) == 0x7F800000u ? u : ((u + 0x1000u) & 0xFFFFE000u);
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(__uint_as_float(u)));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t tf32_lo_bits(uint32_t u, uint32_t hi) {
