@@ -414,6 +414,12 @@ void tma_stages(int bn, bool use_s, int table_entries, int max_smem, int* raw_st
   const TmaSmem fixed = tma_smem_plan(bn, 0, q, table_entries, b_res_kb);
   int r = (int)((max_smem - (int)fixed.total) / (int)fixed.raw_bytes);
   if (r > kTmaMaxStages) r = kTmaMaxStages;
+  // An even ring: k-block i goes to converter group i % 2 and raw stage i % R,
+  // so with R even every stage is always read by the same group, whose
+  // successive parity waits on it are then one phase apart.  With R odd a group
+  // would wait two phases after its previous use and could mistake the older
+  // completed phase of the same parity for the load it waits for.
+  r &= ~1;
   *raw_stages = r;
   *op_stages = q;
 }
@@ -467,7 +473,7 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   if (splits == 1 && K <= (int64_t)kTmaMaxResKB * BK && grid / nt * nt > 0 &&
       ceil_div(K, BK) * 2 * (int64_t)bn * BK * 4 <= kTmaMaxResBytes) {
     tma_stages(bn, use_s, table, d->max_smem_optin, &raw_stages, &op_stages, (int)ceil_div(K, BK));
-    if (raw_stages >= 3) {
+    if (raw_stages >= 4) {
       b_res_kb = (int)ceil_div(K, BK);
       grid = (int)(grid / nt * nt);
     }

@@ -166,7 +166,8 @@ __host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_
   s.op_offset = s.raw_bytes * (uint32_t)raw_stages;
   s.epi_offset = s.op_offset + s.op_bytes * (uint32_t)(b_res_kb > 0 ? b_res_kb : op_stages);
   s.bar_offset = s.epi_offset + 4 * (uint32_t)(bn / 32) * kEpiBuf;  // a 32 x BN block per epilogue warp
-  s.table_offset = s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4 + 2) + 16;
+  // the offset table is read as int4: keep it 16-byte aligned
+  s.table_offset = (s.bar_offset + 8 * (2 * kTmaMaxStages + 2 * kTmaMaxOpStages + 4 + 3) + 16 + 15) & ~15u;
   s.total = s.table_offset + 4 * (uint32_t)table_entries + 1024;  // + alignment slack
   return s;
 }
@@ -542,7 +543,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint64_t* chunk_empty = chunk_full + 2;             // [2]
   uint64_t* b_full = chunk_empty + 2;                 // resident B landed
   uint64_t* b_ready = b_full + 1;                     // resident B split (one arrival per converter warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_ready + 1);
+  uint64_t* mma_done = b_ready + 1;                   // every MMA this CTA issued has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
 
@@ -576,6 +578,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     mbar_init(b_full, 1);
     mbar_init(b_ready, kConvWarps);
+    mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&map_a);
     prefetch_map(&map_b);
@@ -782,6 +785,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           mma_commit(&chunk_full[a]);
         }
       }
+      // TMEM is freed at the end of the kernel: after an aborted pipeline the
+      // epilogue may not have waited for the last MMAs, so wait for them here
+      mma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
     }
   } else {
     // ----------------------------------------------------------- epilogue
