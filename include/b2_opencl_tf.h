@@ -278,6 +278,14 @@ int b2_dense(b2_stream_t stream, const float* x, const int64_t x_shape[2],
              const float* w, const int64_t w_shape[2], const float* b,
              int64_t b_len, float* y);
 
+/* OpenclDense then OpenclRelu fused: y = relu(b + x . W), the ReLU applied
+ * where each sum is finished; the same bits as b2_dense then b2_relu.
+ * Replaces the pair src/ops/dense_ops.cc:57-146 + src/ops/relu_ops.cc:40-93
+ * (the README model's Dense(128, activation="relu") head). */
+int b2_dense_relu(b2_stream_t stream, const float* x, const int64_t x_shape[2],
+                  const float* w, const int64_t w_shape[2], const float* b,
+                  int64_t b_len, float* y);
+
 /* OpenclDenseBackpropInput(grad_y, w) -> grad_y . W^T
  * src/ops/dense_ops.cc:152-230 */
 int b2_dense_backprop_input(b2_stream_t stream, const float* grad_y,

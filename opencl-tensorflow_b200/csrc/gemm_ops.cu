@@ -39,7 +39,8 @@ constexpr int kRedParts = 16;
 __global__ void __launch_bounds__(32 * kRedParts) splitk_reduce_kernel(const float* __restrict__ part, int splits,
                                                                        int64_t M, int64_t N,
                                                                        const float* __restrict__ bias,
-                                                                       float* __restrict__ out, int64_t ldo) {
+                                                                       float* __restrict__ out, int64_t ldo,
+                                                                       int relu) {
   __shared__ float s_part[kRedParts][32];
   const int64_t total = M * N;
   const int64_t i = (int64_t)blockIdx.x * 32 + threadIdx.x;
@@ -55,7 +56,7 @@ __global__ void __launch_bounds__(32 * kRedParts) splitk_reduce_kernel(const flo
     for (int j = 1; j < kRedParts; ++j) sum += s_part[j][threadIdx.x];
     const int64_t m = i / N, n = i - m * N;
     if (bias) sum += bias[n];
-    out[m * ldo + n] = sum;
+    out[m * ldo + n] = relu && !(sum > 0.0f) ? 0.0f : sum;
   }
 }
 
@@ -452,7 +453,7 @@ struct ASpec {
 inline ASpec a_matrix(const MatOperand& m) { return ASpec{m.k_major ? kAK : kAMN, m, nullptr, 0, ConvRows{}}; }
 
 int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int64_t K, float* out,
-                 const float* bias, cudaStream_t s, const char* name, int min_kb_per_split) {
+                 const float* bias, cudaStream_t s, const char* name, int min_kb_per_split, bool relu = false) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   const int bn = tma_bn(N);
@@ -481,7 +482,8 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   if (b_res_kb == 0) tma_stages(bn, use_s, table, d->max_smem_optin, &raw_stages, &op_stages);
   if (raw_stages < 2 || op_stages < 2)
     return set_error(B2_ERR_INTERNAL, "%s: shared memory too small for the TMA engine", name);
-  TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4, b_res_kb};
+  TmaProblem prob{a.cr, M, N, K, kps, splits, bn, bias, false, use_s, (uint32_t)BM * BK * 4, relu && splits == 1,
+                  b_res_kb};
   B2_REQUIRE(tiles * splits <= kMaxInt32, "%s: too many output tiles", name);
   prob.nt_div = FastDiv((uint32_t)nt);
   prob.mt_div = FastDiv((uint32_t)ceil_div(M, BM));
@@ -536,7 +538,8 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   }
   B2_RETURN_IF_ERROR(rc);
   if (splits == 1) return B2_OK;
-  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N,
+                                                                                   bias, out, N, relu ? 1 : 0);
   return check_launch(s, "splitk_reduce");
 }
 
@@ -573,7 +576,7 @@ bool tma_output_ok(const float* out, int64_t M, int64_t N) {
 
 template <class AV, class BV>
 int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* out, const float* bias,
-             cudaStream_t s, const char* name, int min_kb_per_split = 4) {
+             cudaStream_t s, const char* name, int min_kb_per_split = 4, bool relu = false) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   if (M == 0 || N == 0) return B2_OK;
@@ -581,7 +584,7 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
     const MatOperand ma = mat_of(a), mb = mat_of(b);
     if (K > 0 && tma_engine_enabled() && tma_operand_ok(ma, K) && tma_operand_ok(mb, K) && aligned16(out) &&
         N % 4 == 0 && M <= kI32 && N <= kI32)
-      return run_tma_gemm(a_matrix(ma), mb, M, N, K, out, bias, s, name, min_kb_per_split);
+      return run_tma_gemm(a_matrix(ma), mb, M, N, K, out, bias, s, name, min_kb_per_split, relu);
   }
   const int bn = choose_bn(N);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
@@ -590,12 +593,17 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
   if (kps < BK) kps = BK;
   splits = (int)(K > 0 ? ceil_div(K, kps) : 1);
   GemmProblem<AV, BV> prob{a, b, M, N, K, kps, splits, Epilogue{out, N, bias, false}};
-  if (splits == 1) return launch_gemm(prob, bn, s, name);
+  if (splits == 1) {
+    B2_RETURN_IF_ERROR(launch_gemm(prob, bn, s, name));
+    // this engine's epilogue has no ReLU: apply it in place
+    return relu ? b2_relu(s, out, out, M * N) : B2_OK;
+  }
   Scratch part;
   B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)splits * M * N, s));
   prob.ep = Epilogue{part.as<float>(), N, nullptr, true};
   B2_RETURN_IF_ERROR(launch_gemm(prob, bn, s, name));
-  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N, bias, out, N);
+  splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, 32), dim3(32, kRedParts), 0, s>>>(part.as<float>(), splits, M, N, bias,
+                                                                                   out, N, relu ? 1 : 0);
   return check_launch(s, "splitk_reduce");
 }
 
@@ -770,6 +778,23 @@ int b2_dense(b2_stream_t stream, const float* x, const int64_t x_shape[2], const
   const KContig av{x, batch, in_f, aligned16(x) && in_f % 4 == 0};
   const MNMajor bv{w, out_f, out_f};
   return run_gemm(av, bv, batch, out_f, in_f, y, b, s, "dense_forward");
+}
+
+// OpenclDense followed by OpenclRelu (src/ops/dense_ops.cc:57-140, src/ops/relu_ops.cc):
+// relu(x W + b) with the ReLU applied where the sum is finished (the GEMM
+// epilogue or the split-K reduction), the same bits as the two ops in sequence.
+int b2_dense_relu(b2_stream_t stream, const float* x, const int64_t x_shape[2], const float* w,
+                  const int64_t w_shape[2], const float* b, int64_t b_len, float* y) {
+  clear_error();
+  B2_REQUIRE(x_shape && w_shape, "x must be rank 2");
+  const int64_t batch = x_shape[0], in_f = x_shape[1], out_f = w_shape[1];
+  B2_REQUIRE(batch >= 0 && in_f >= 0 && out_f >= 0 && w_shape[0] >= 0, "dimensions must be non-negative");
+  B2_REQUIRE(w_shape[0] == in_f, "W[0] must equal x[1] (in_features)");
+  B2_REQUIRE(b_len == out_f, "b[0] must equal W[1] (out_features)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const KContig av{x, batch, in_f, aligned16(x) && in_f % 4 == 0};
+  const MNMajor bv{w, out_f, out_f};
+  return run_gemm(av, bv, batch, out_f, in_f, y, b, s, "dense_relu_forward", 4, true);
 }
 
 // src/ops/dense_ops.cc:170-227

@@ -129,6 +129,7 @@ struct TmaProblem {
   bool partial;       // out is [splits][M][N] partials (3-D store map)
   bool use_s;         // some tile spans several chunks: keep a running sum S
   uint32_t a_tx;      // bytes of the raw A load per k-block (<= 16 KB)
+  bool relu;          // direct mode: the output is relu(sum + bias)
   int b_res_kb;       // > 0: every tile of a CTA shares one B tile of this many
                       // k-blocks, loaded and split once and kept in shared memory
   FastDiv nt_div, mt_div;  // N tiles, M tiles (tile indices < 2^31)
@@ -848,6 +849,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (n + e < p.N) v[e] += __ldg(p.bias + n + e);
+          }
+          if (p.relu) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = v[e] > 0.0f ? v[e] : 0.0f;  // fmax(v, 0): NaN -> 0, -0 -> +0
           }
           uint8_t* buf = ebuf + (c / 32) * kEpiBuf;  // 32 x 32 block, 128-byte swizzled rows
 #pragma unroll

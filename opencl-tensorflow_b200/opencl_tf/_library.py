@@ -74,6 +74,7 @@ _SIGS = {
     "b2_batch_norm_relu_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P, _P, _P, _F32, _F32],
     "b2_batch_norm_relu_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
     "b2_dense": [_P, _P, _P, _P, _P, _P, _I64, _P],
+    "b2_dense_relu": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_backprop_input": [_P, _P, _P, _P, _P, _P],
     "b2_dense_backprop_weight": [_P, _P, _P, _P, _P, _P],
     "b2_dense_backprop_bias": [_P, _P, _P, _P],
@@ -412,7 +413,7 @@ def _k_batch_norm_grad(grad_y, x, gamma, saved_mean, saved_var, epsilon=1e-3):
     return dx, dg, db
 
 
-def _k_dense(x, w, b):
+def _dense_call(x, w, b, relu):
     x = _input(x, "x")
     w = _input(w, "W")
     b = _input(b, "b")
@@ -420,10 +421,18 @@ def _k_dense(x, w, b):
     _rank(w, 2, "W must be rank 2")
     _rank(b, 1, "b must be rank 1")
     y = torch.empty((x.shape[0], w.shape[1]), device=x.device, dtype=torch.float32)
+    entry = _lib.b2_dense_relu if relu else _lib.b2_dense
     with _on_device(x):
-        _check(_lib.b2_dense(_stream(x), _p(x), _I64x2(*x.shape), _p(w), _I64x2(*w.shape), _p(b), b.shape[0],
-                             _p(y)))
+        _check(entry(_stream(x), _p(x), _I64x2(*x.shape), _p(w), _I64x2(*w.shape), _p(b), b.shape[0], _p(y)))
     return y
+
+
+def _k_dense(x, w, b):
+    return _dense_call(x, w, b, False)
+
+
+def _k_dense_relu(x, w, b):
+    return _dense_call(x, w, b, True)
 
 
 def _k_dense_backprop_input(grad_y, w):
@@ -716,14 +725,19 @@ def _mk_fused_ops():
     def opencl_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, epsilon=1e-3):
         return _k_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, float(epsilon))
 
+    def opencl_dense_relu(x, w, b):
+        """relu(x @ W + b) with the ReLU in the GEMM's epilogue."""
+        return _apply("OpenclDenseRelu", _k_dense_relu, (x, w, b), {})
+
     ns.opencl_batch_norm_relu_training = opencl_batch_norm_relu_training
     ns.opencl_batch_norm_relu_grad = opencl_batch_norm_relu_grad
+    ns.opencl_dense_relu = opencl_dense_relu
     return ns
 
 
 fused_ops = _mk_fused_ops()
 """Ops with no counterpart in the reference: pairs its layers run back to back
-(BatchNormTraining -> Relu), fused, with bit-identical results."""
+(BatchNormTraining -> Relu, Dense -> Relu), fused, with bit-identical results."""
 
 
 def _mk_step_ops():

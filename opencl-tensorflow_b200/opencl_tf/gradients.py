@@ -91,6 +91,20 @@ def _dense_grad(op, grad):
     return [dx, dw, db]
 
 
+@RegisterGradient("OpenclDenseRelu")
+def _dense_relu_grad(op, grad):
+    """ReluGrad then the three dense gradients.  The mask is taken from the
+    op's output z = relu(x W + b): z > 0 exactly where x W + b > 0 (NaN gives
+    z = 0 and fails both tests), so the bits equal those of the unfused pair."""
+    x, w, _b = op.inputs
+    g = raw_ops.opencl_relu_grad(grad, op.outputs[0])
+    need_x, need_w, need_b = op.needs_input_grad
+    dx = raw_ops.opencl_dense_backprop_input(g, w) if need_x else None
+    dw = raw_ops.opencl_dense_backprop_weight(x, g) if need_w else None
+    db = raw_ops.opencl_dense_backprop_bias(g) if need_b else None
+    return [dx, dw, db]
+
+
 @RegisterGradient("OpenclUpsamplingBilinear2d")
 def _upsampling_bilinear_grad(op, grad):
     return [raw_ops.opencl_upsampling_bilinear2d_grad(grad, _host_shape(op.inputs[0]), size=op.get_attr("size"))]

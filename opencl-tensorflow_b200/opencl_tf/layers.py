@@ -220,10 +220,17 @@ class OpenCLDense(_Layer):
             self.bias = self._weight("bias", (self.units,), self.bias_initializer)
         super().build(input_shape)
 
+    def _b(self, x):
+        return self.bias if self.use_bias else torch.zeros((self.units,), dtype=x.dtype, device=x.device)
+
     def forward(self, x):
-        if self.use_bias:
-            return dense(x, self.kernel, self.bias)
-        return dense(x, self.kernel, torch.zeros((self.units,), dtype=x.dtype, device=x.device))
+        return dense(x, self.kernel, self._b(x))
+
+    def forward_relu(self, x):
+        """relu(self(x)): this layer followed by an OpenCLReLU as one op, the
+        ReLU applied in the GEMM's epilogue (bit-identical values and
+        gradients, one launch and one pass over the output fewer)."""
+        return _library.fused_ops.opencl_dense_relu(x, self.kernel, self._b(x))
 
     def get_config(self):
         cfg = super().get_config()

@@ -6,9 +6,10 @@ built from this package's layers:
     dsconv_block(144, strides=2)
     Flatten -> Dense(128) -> ReLU -> Reshape(4, 4, 8) -> UpSampling2D(2x) -> Sigmoid
 
-Each BatchNormalization -> ReLU pair runs as one fused op in training
-(``fuse_bn_relu=True``, the default): the same values and gradients bit for
-bit as the two layers in sequence, one activation pass fewer each way.
+Each BatchNormalization -> ReLU pair runs as one fused op in training, and
+Dense -> ReLU as one GEMM with the ReLU in its epilogue (``fuse_bn_relu=True``,
+the default): the same values and gradients bit for bit as the layers in
+sequence, one activation pass fewer each way.
 
 ``build_model(widened=True)`` gives the larger variant used for scaling runs:
 input 256x256x3, filters 96/192/288, Dense 512, Reshape(8, 8, 8) -> 16x16x8.
@@ -80,7 +81,7 @@ class BuildModel(nn.Module):
             x = self._bn_relu(bn1, r1, dw(x), training)
             x = self._bn_relu(bn2, r2, pw(x), training)
         x = x.reshape(x.shape[0], -1)
-        x = self.dense_relu(self.dense(x))
+        x = self.dense.forward_relu(x) if self.fuse_bn_relu else self.dense_relu(self.dense(x))
         x = x.reshape(x.shape[0], *self.head)
         return self.sigmoid(self.up(x))
 

@@ -27,7 +27,7 @@ from . import _library as L
 _KERNELS = ["_k_conv2d", "_k_conv2d_backprop_input", "_k_conv2d_backprop_filter", "_k_depthwise_conv2d",
             "_k_depthwise_conv2d_backprop_input", "_k_depthwise_conv2d_backprop_filter", "_k_relu", "_k_relu_grad",
             "_k_sigmoid", "_k_sigmoid_grad", "_k_batch_norm_training", "_k_batch_norm_inference",
-            "_k_batch_norm_grad", "_k_dense", "_k_dense_backprop_input", "_k_dense_backprop_weight",
+            "_k_batch_norm_grad", "_k_dense", "_k_dense_relu", "_k_dense_backprop_input", "_k_dense_backprop_weight",
             "_k_dense_backprop_bias", "_k_upsampling_bilinear2d", "_k_upsampling_bilinear2d_grad",
             "_k_batch_norm_relu_training", "_k_batch_norm_relu_grad", "_k_mse_loss", "_k_mse_loss_grad"]
 
@@ -98,7 +98,7 @@ def work(name, args, kw, out) -> tuple[float, float]:
         taps = w.shape[0] * w.shape[1]
         big = outs[0] if name == "depthwise_conv2d" else args[2]
         flops = 2.0 * big.numel() * taps
-    elif name == "dense":
+    elif name in ("dense", "dense_relu"):
         x, w = args[0], args[1]
         flops = 2.0 * x.shape[0] * x.shape[1] * w.shape[1]
     elif name == "dense_backprop_input":

@@ -38,7 +38,7 @@ def test_gradient_registry_matches_reference_wiring():
                  "OpenclDense", "OpenclUpsamplingBilinear2d"}
     # the reference's registrations, plus the extensions (not reference ops): the fused
     # BatchNorm -> ReLU pair and the training step's MSE loss
-    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining", "OpenclMseLoss"}
+    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining", "OpenclDenseRelu", "OpenclMseLoss"}
     assert "OpenclBatchNormInference" not in _GRADIENTS
 
 

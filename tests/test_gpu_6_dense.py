@@ -57,6 +57,47 @@ def test_dense_gradient_via_autograd(otf, port):
     assert_close(to_np(bt.grad), port.dense_backprop_bias(ry), what="db")
 
 
+def _bits(t):
+    return t.detach().contiguous().view(torch.int32)
+
+
+@pytest.mark.parametrize("batch,in_f,out_f", [(256, 1152, 128),  # the README head: TMA engine, one split
+                                              (257, 2052, 132),  # TMA engine, split-K reduce
+                                              (130, 300, 270),   # fallback engine, one split (in-place ReLU)
+                                              (2, 4097, 17),     # fallback engine, split-K reduce
+                                              (5, 0, 3), (1, 1, 1)])
+def test_dense_relu_matches_pair(otf, batch, in_f, out_f):
+    """The fused Dense -> ReLU against OpenclDense then OpenclRelu: the same
+    bits forward (NaN rows included) and backward."""
+    from opencl_tf._library import fused_ops, raw_ops
+    rng = np.random.default_rng(batch + in_f + out_f)
+    x = rng.standard_normal((batch, in_f)).astype(np.float32)
+    if in_f:
+        x[0, 0] = np.nan  # row 0 of the sum is NaN; ReLU maps it to 0 on both paths
+    W = rng.standard_normal((in_f, out_f)).astype(np.float32)
+    b = rng.standard_normal((out_f,)).astype(np.float32)
+    dz = _cuda(rng.standard_normal((batch, out_f)))
+    fused = [_cuda(a).requires_grad_(True) for a in (x, W, b)]
+    pair = [_cuda(a).requires_grad_(True) for a in (x, W, b)]
+    zf = fused_ops.opencl_dense_relu(*fused)
+    zp = raw_ops.opencl_relu(raw_ops.opencl_dense(*pair))
+    assert torch.equal(_bits(zf), _bits(zp))
+    assert not torch.isnan(zf).any()
+    zf.backward(dz)
+    zp.backward(dz)
+    for a, c, what in zip(fused, pair, ("dx", "dW", "db")):
+        assert torch.equal(_bits(a.grad), _bits(c.grad)), what
+
+
+def test_dense_relu_bad_args(otf):
+    from opencl_tf._library import fused_ops
+    x = torch.zeros(2, 3, device="cuda")
+    with pytest.raises(otf.errors.InvalidArgumentError, match="in_features"):
+        fused_ops.opencl_dense_relu(x, torch.zeros(4, 5, device="cuda"), torch.zeros(5, device="cuda"))
+    with pytest.raises(otf.errors.InvalidArgumentError, match="out_features"):
+        fused_ops.opencl_dense_relu(x, torch.zeros(3, 5, device="cuda"), torch.zeros(4, device="cuda"))
+
+
 def test_stress_gemm_reduced(otf):
     """The stress GEMM's shape family (M=8192, K=N=4096 at full size) at a
     quarter of each dimension, against float64."""
