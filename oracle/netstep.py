@@ -115,3 +115,175 @@ def train_grads_f64(p, x, target, head=(4, 4, 8), up=(2, 2), eps=1e-3, device="c
     g = {k: P[k].grad.cpu().numpy() for k in P}
     g["blocks"] = [{k: v.grad.cpu().numpy() for k, v in b.items()} for b in Bl]
     return float(loss), out.detach().cpu().numpy(), g
+
+
+# ---------------------------------------------------------------------------
+# Any network given as a stage list (opencl_tf.model: BuildModel.stages(),
+# UwbLocV3.stages()): the forward pass, MSE loss and backward pass with the
+# reference's gradient wiring (opencl_tf/gradients.py:18-119), and the
+# inference forward with BatchNormalization on its moving statistics.
+
+def seq_of(model):
+    """The model's stages as plain data: (kind, params, arg) with numpy weights
+    (conv/dw/dense: w [, b]; bn: g, b, mean, var, eps) and the strides,
+    upsampling size or reshape target as arg."""
+    out = []
+    for kind, layer, arg in model.stages():
+        if kind in ("conv", "dw"):
+            s = layer.strides
+            out.append((kind, {"w": _np(layer.kernel)}, ((1, s[0], s[1], 1), layer.padding)))
+        elif kind == "bn":
+            out.append((kind, {"g": _np(layer.gamma), "b": _np(layer.beta), "mean": _np(layer.moving_mean),
+                               "var": _np(layer.moving_var)}, float(layer.epsilon)))
+        elif kind == "dense":
+            b = _np(layer.bias) if layer.use_bias else np.zeros(layer.units, np.float32)
+            out.append((kind, {"w": _np(layer.kernel), "b": b}, None))
+        elif kind == "up":
+            out.append((kind, {}, tuple(layer.size)))
+        else:
+            out.append((kind, {}, arg))
+    return out
+
+
+def uwb_input(x):
+    """Permute((1, 4, 2, 3, 5)) + Reshape((T, bins, 36)) of the uwb_loc_v3 input."""
+    n, t, _, _, bins, _ = x.shape
+    return np.ascontiguousarray(np.transpose(x, (0, 1, 4, 2, 3, 5))).reshape(n, t, bins, 36)
+
+
+def seq_forward_inference(o, seq, x):
+    """Inference forward: BatchNormalization -> OpenclBatchNormInference with
+    the moving statistics."""
+    a = x
+    for kind, p, arg in seq:
+        if kind == "conv":
+            a = o.conv2d(a, p["w"], arg[0], arg[1])
+        elif kind == "dw":
+            a = o.depthwise_conv2d(a, p["w"], arg[0], arg[1])
+        elif kind == "bn":
+            a = o.batch_norm_inference(a, p["g"], p["b"], p["mean"], p["var"], arg)
+        elif kind == "relu":
+            a = o.relu(a)
+        elif kind == "dense":
+            a = o.dense(a, p["w"], p["b"])
+        elif kind == "flatten":
+            a = a.reshape(a.shape[0], -1)
+        elif kind == "reshape":
+            a = a.reshape(a.shape[0], *arg)
+        elif kind == "up":
+            a = o.upsampling_bilinear_2d(a, arg)
+        elif kind == "sigmoid":
+            a = o.sigmoid(a)
+        else:
+            raise ValueError(kind)
+    return a
+
+
+def seq_train_grads(o, seq, x, target):
+    """Training step: returns (loss, out, grads) with grads[i] a dict of the
+    i-th stage's weight gradients (conv/dw: w; bn: g, b; dense: w, b)."""
+    acts, saved = [], []
+    a = x
+    for kind, p, arg in seq:
+        acts.append(a)
+        if kind == "conv":
+            a = o.conv2d(a, p["w"], arg[0], arg[1])
+        elif kind == "dw":
+            a = o.depthwise_conv2d(a, p["w"], arg[0], arg[1])
+        elif kind == "bn":
+            a, m, v = o.batch_norm_training(a, p["g"], p["b"], arg)
+            saved.append((m, v))
+        elif kind == "relu":
+            a = o.relu(a)
+        elif kind == "dense":
+            a = o.dense(a, p["w"], p["b"])
+        elif kind in ("flatten", "reshape"):
+            a = a.reshape(a.shape[0], -1) if kind == "flatten" else a.reshape(a.shape[0], *arg)
+        elif kind == "up":
+            a = o.upsampling_bilinear_2d(a, arg)
+        elif kind == "sigmoid":
+            a = o.sigmoid(a)
+        else:
+            raise ValueError(kind)
+    out = a
+    diff = out.astype(np.float64) - target.astype(np.float64)
+    loss = float(np.mean(diff * diff))
+    d = (2.0 * diff / diff.size).astype(np.float32)
+    grads = [dict() for _ in seq]
+    bn_i = len(saved)
+    for i in range(len(seq) - 1, -1, -1):
+        kind, p, arg = seq[i]
+        xin = acts[i]
+        if kind == "conv":
+            grads[i]["w"] = o.conv2d_backprop_filter(xin, p["w"].shape, d, arg[0], arg[1])
+            d = o.conv2d_backprop_input(xin.shape, p["w"], d, arg[0], arg[1]) if i else None
+        elif kind == "dw":
+            grads[i]["w"] = o.depthwise_conv2d_backprop_filter(xin, p["w"].shape, d, arg[0], arg[1])
+            d = o.depthwise_conv2d_backprop_input(xin.shape, p["w"], d, arg[0], arg[1]) if i else None
+        elif kind == "bn":
+            bn_i -= 1
+            m, v = saved[bn_i]
+            d, grads[i]["g"], grads[i]["b"] = o.batch_norm_grad(d, xin, p["g"], m, v, arg)
+        elif kind == "relu":
+            d = o.relu_grad(d, xin)
+        elif kind == "dense":
+            grads[i]["w"] = o.dense_backprop_weight(xin, d)
+            grads[i]["b"] = o.dense_backprop_bias(d)
+            d = o.dense_backprop_input(d, p["w"])
+        elif kind in ("flatten", "reshape"):
+            d = d.reshape(xin.shape)
+        elif kind == "up":
+            d = o.upsampling_bilinear_2d_grad(d, xin.shape, arg)
+        elif kind == "sigmoid":
+            d = o.sigmoid_grad(acts[i + 1] if i + 1 < len(acts) else out, d)
+    return loss, out, grads
+
+
+def seq_train_grads_f64(seq, x, target, device="cpu"):
+    """The same training step in float64 torch autograd (TF SAME padding,
+    biased-variance BN, half-pixel bilinear) -- the exact arbiter."""
+    import torch
+    import torch.nn.functional as F
+
+    dev = torch.device(device)
+    tt = lambda a: torch.tensor(np.asarray(a), dtype=torch.float64, device=dev, requires_grad=True)  # noqa: E731
+    P = [{k: tt(v) for k, v in p.items() if k in ("w", "b", "g")} for _, p, _ in seq]
+
+    def conv(z, w, strides, padding, groups=1):
+        kh, kw = w.shape[0], w.shape[1]
+        sh, sw = strides[1], strides[2]
+        H, W = z.shape[2], z.shape[3]
+        if padding == "SAME":
+            oh, ow = -(-H // sh), -(-W // sw)
+            ph = max((oh - 1) * sh + kh - H, 0)
+            pw = max((ow - 1) * sw + kw - W, 0)
+            z = F.pad(z, (pw // 2, pw - pw // 2, ph // 2, ph - ph // 2))
+        wt = w.permute(3, 2, 0, 1) if groups == 1 else w.permute(2, 3, 0, 1).reshape(-1, 1, kh, kw)
+        return F.conv2d(z, wt, stride=(sh, sw), groups=groups)
+
+    z = torch.tensor(x, dtype=torch.float64, device=dev).permute(0, 3, 1, 2)  # NCHW while spatial
+    for (kind, p, arg), q in zip(seq, P):
+        if kind == "conv":
+            z = conv(z, q["w"], arg[0], arg[1])
+        elif kind == "dw":
+            z = conv(z, q["w"], arg[0], arg[1], groups=z.shape[1])
+        elif kind == "bn":
+            m = z.mean(dim=(0, 2, 3), keepdim=True)
+            v = (z * z).mean(dim=(0, 2, 3), keepdim=True) - m * m
+            z = q["g"].view(1, -1, 1, 1) * (z - m) / torch.sqrt(v + arg) + q["b"].view(1, -1, 1, 1)
+        elif kind == "relu":
+            z = torch.relu(z)
+        elif kind == "flatten":
+            z = z.permute(0, 2, 3, 1).reshape(z.shape[0], -1)
+        elif kind == "dense":
+            z = z @ q["w"] + q["b"]
+        elif kind == "reshape":
+            z = z.reshape(z.shape[0], *arg).permute(0, 3, 1, 2)
+        elif kind == "up":
+            z = F.interpolate(z, scale_factor=arg, mode="bilinear", align_corners=False)
+        elif kind == "sigmoid":
+            z = torch.sigmoid(z)
+    out = z.permute(0, 2, 3, 1)
+    loss = torch.mean((out - torch.tensor(target, dtype=torch.float64, device=dev)) ** 2)
+    loss.backward()
+    return float(loss), out.detach().cpu().numpy(), [{k: v.grad.cpu().numpy() for k, v in q.items()} for q in P]
