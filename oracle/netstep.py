@@ -286,4 +286,4 @@ def seq_train_grads_f64(seq, x, target, device="cpu"):
     out = z.permute(0, 2, 3, 1)
     loss = torch.mean((out - torch.tensor(target, dtype=torch.float64, device=dev)) ** 2)
     loss.backward()
-    return float(loss), out.detach().cpu().numpy(), [{k: v.grad.cpu().numpy() for k, v in q.items()} for q in P]
+    return float(loss.detach()), out.detach().cpu().numpy(), [{k: v.grad.cpu().numpy() for k, v in q.items()} for q in P]
