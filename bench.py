@@ -2,6 +2,7 @@
 """Throughput of the README ``build_model()`` training step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--widened]
+                    [--model build_model|uwb_loc_v3]
 
 One step = forward + MSE loss + backward (the 19 custom ops) + gradient
 averaging across ranks + Adam, on a fixed synthetic batch of 256 images per
@@ -24,6 +25,8 @@ Reported (one JSON line from rank 0):
             oracle/_ref) running the same step on all host cores, on a bounded
             sample of the batch.
 ``--impl reference`` times only that CPU implementation (rank 0).
+``--model uwb_loc_v3`` measures the second network instead (the reference's
+examples/train_full_model.py model; 1024 samples of stacked IQ per GPU).
 """
 from __future__ import annotations
 
@@ -45,24 +48,43 @@ sys.path.insert(0, str(ROOT / "opencl-tensorflow_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "build_model train images/s at 1/2/4/8 B200; per-op % of HBM/TC roofline"
+METRIC_UWB = "uwb_loc_v3 train samples/s; per-op % of HBM/TC roofline"
 PER_GPU_BATCH = 256
 
 
-def workload(widened: bool) -> dict:
+def workload(widened: bool, model: str = "build_model") -> dict:
+    if model == "uwb_loc_v3":
+        return {"workload": "uwb_loc_v3 training step (examples/train_full_model.py): stacked IQ [8,6,3,16,2] -> "
+                            "[8,16,36], conv 48 (3,7)/(1,2), dsconv 96/144/192 stride 2, neck 64, Dense 432, head "
+                            "9x6x8 -> up, conv 16 -> up, conv 16 -> 36x24x1; fwd+bwd+Adam(1e-3), MSE",
+                "batch_per_gpu": 1024, "model": model, "metric": METRIC_UWB, "cpu_sample": 64, "unit": "samples/s"}
     if widened:
         return {"workload": "README build_model training step, widened: input 256x256x3, filters 96/192/288, "
                             "Dense 512, head 8x8x8 -> 16x16x8; fwd+bwd+Adam(1e-3), MSE",
-                "batch_per_gpu": 128, "in_hw": 256, "out_hw": 16}
+                "batch_per_gpu": 128, "in_hw": 256, "out_hw": 16, "model": model, "metric": METRIC, "cpu_sample": 1, "unit": "images/s"}
     return {"workload": "README build_model training step: input 64x64x3, conv 48 (3,7)/(1,2), dsconv 96 and 144 "
                         "stride 2, Dense 128, head 4x4x8 -> 8x8x8; fwd+bwd+Adam(1e-3), MSE",
-            "batch_per_gpu": PER_GPU_BATCH, "in_hw": 64, "out_hw": 8}
+            "batch_per_gpu": PER_GPU_BATCH, "in_hw": 64, "out_hw": 8, "model": model, "metric": METRIC,
+            "cpu_sample": 16, "unit": "images/s"}
 
 
-def make_batch(n, in_hw, out_hw, seed):
+def make_batch(w, n, seed):
     rng = np.random.default_rng(seed)
+    if w["model"] == "uwb_loc_v3":  # the example's make_batch: IQ ~ N(0, 1), heatmap ~ U(0, 1)
+        x = rng.standard_normal((n, 8, 6, 3, 16, 2)).astype(np.float32)
+        t = rng.uniform(0, 1, (n, 36, 24, 1)).astype(np.float32)
+        return x, t
+    in_hw, out_hw = w["in_hw"], w["out_hw"]
     x = rng.uniform(0, 1, (n, in_hw, in_hw, 3)).astype(np.float32)
     t = rng.uniform(0, 1, (n, out_hw, out_hw, 8)).astype(np.float32)
     return x, t
+
+
+def build_net(w, widened, device=None):
+    from opencl_tf.model import build_model, build_uwb_loc_v3
+    if w["model"] == "uwb_loc_v3":
+        return build_uwb_loc_v3(device=device)
+    return build_model(widened=widened, device=device)
 
 
 # ------------------------------------------------------------------ clocks
@@ -149,27 +171,35 @@ def _flat(p, prefix=""):
     return out
 
 
-def cpu_reference_steps(widened, sample_images, steps, warmup, min_seconds=0.0):
+def cpu_reference_steps(widened, sample_images, steps, warmup, min_seconds=0.0, model_name="build_model"):
     """Runs the training step with the reference's host-compiled kernels;
     returns (images/s, cores, kind, seconds, steps_done)."""
     import torch
-    from oracle.netstep import params_of, train_grads
+    from oracle.netstep import params_of, seq_of, seq_train_grads, train_grads, uwb_input
     from oracle.oracle import Oracle, available
-    from opencl_tf.model import build_model
     kind = "reference" if available("ref") else "port"
     o = Oracle("ref" if kind == "reference" else "port")
     torch.manual_seed(0)
-    model = build_model(widened=widened)
-    p = params_of(model)
-    w = workload(widened)
-    x, t = make_batch(sample_images, w["in_hw"], w["out_hw"], 1234)
-    head = (8, 8, 8) if widened else (4, 4, 8)
-    flat = _flat(p)
+    w = workload(widened, model_name)
+    model = build_net(w, widened)
+    x, t = make_batch(w, sample_images, 1234)
     state = {}
+    if model_name == "uwb_loc_v3":
+        seq = seq_of(model)
+        xi = uwb_input(x)
+        flat = {f"{i}.{k}": v for i, (_, p, _) in enumerate(seq) for k, v in p.items() if k in ("w", "b", "g")}
 
-    def step():
-        _, _, g = train_grads(o, p, x, t, head=head)
-        adam_np(flat, _flat(g), state)
+        def step():
+            _, _, g = seq_train_grads(o, seq, xi, t)
+            adam_np(flat, {f"{i}.{k}": v for i, d in enumerate(g) for k, v in d.items()}, state)
+    else:
+        p = params_of(model)
+        head = (8, 8, 8) if widened else (4, 4, 8)
+        flat = _flat(p)
+
+        def step():
+            _, _, g = train_grads(o, p, x, t, head=head)
+            adam_np(flat, _flat(g), state)
 
     for _ in range(warmup):
         step()
@@ -204,16 +234,15 @@ def run_ours(args, rank, world, local_rank):
 
     import opencl_tf
     from opencl_tf import profile
-    from opencl_tf.model import build_model
     from opencl_tf.train import TrainStep
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    w = workload(args.widened)
+    w = workload(args.widened, args.model)
     B = w["batch_per_gpu"]
     torch.manual_seed(0)
-    model = build_model(widened=args.widened, device=dev)
-    x_np, t_np = make_batch(B, w["in_hw"], w["out_hw"], 1000 + rank)
+    model = build_net(w, args.widened, device=dev)
+    x_np, t_np = make_batch(w, B, 1000 + rank)
     x_dev = torch.from_numpy(x_np).to(dev)
     t_dev = torch.from_numpy(t_np).to(dev)
     step = TrainStep(model, lr=1e-3, graphed=True, warmup=3)
@@ -339,22 +368,23 @@ def run_ours(args, rank, world, local_rank):
     # ---- CPU baseline (rank 0 at N=1 only; bounded sample)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, 16 if not args.widened else 1, 1, 1,
-                                                             min_seconds=10.0)
-        cpu = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": kind,
-               "sample": f"{nsteps} training steps of {16 if not args.widened else 1} images (of the {B}-image "
+        ns = w["cpu_sample"]
+        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, ns, 1, 1, min_seconds=10.0,
+                                                             model_name=args.model)
+        cpu = {"value": round(ips, 3), "unit": w["unit"], "cores": cores, "kind": kind,
+               "sample": f"{nsteps} training steps of {ns} images (of the {B}-image "
                          f"batch) through the host-compiled reference kernels, {secs:.1f} s"}
 
     images = B * world * args.steps
     line = {
-        "metric": METRIC, "value": round(images / (ms_dev * 1e-3), 2), "unit": "images/s", "n_gpus": world,
+        "metric": w["metric"], "value": round(images / (ms_dev * 1e-3), 2), "unit": w["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": w["workload"], "global_batch": B * world, "per_gpu_batch": B,
                    "parallelism": f"dp{world}", "cuda_graph": True,
                    "l2": "flushed between timed steps (256 MiB write outside the step's events)",
                    "math": "fp32 activations; contractions on tcgen05 tensor cores in 3xTF32"},
-        "e2e": {"value": round(images / (ms_e2e * 1e-3), 2), "unit": "images/s",
+        "e2e": {"value": round(images / (ms_e2e * 1e-3), 2), "unit": w["unit"],
                 "h2d_bytes_per_step": int(x_host.numel() * 4 + t_host.numel() * 4), "d2h_bytes_per_step": 4,
                 "ms_per_step": round(ms_e2e / args.steps, 4),
                 "pipeline": "next batch copied host->device on a copy stream during the step; each step's "
@@ -375,6 +405,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--widened", action="store_true")
+    ap.add_argument("--model", choices=["build_model", "uwb_loc_v3"], default="build_model")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -382,23 +413,24 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    w = workload(args.widened)
+    w = workload(args.widened, args.model)
 
     if args.impl == "reference":
         if rank != 0:
             return 0
-        sample = 16 if not args.widened else 1
-        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, sample, args.steps, args.warmup)
-        line = {"metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
+        sample = w["cpu_sample"]
+        ips, cores, kind, secs, nsteps = cpu_reference_steps(args.widened, sample, args.steps, args.warmup,
+                                                             model_name=args.model)
+        line = {"metric": w["metric"], "value": round(ips, 3), "unit": w["unit"], "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / nsteps * 1e3, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "impl": "reference",
                 "config": {"workload": w["workload"], "global_batch": w["batch_per_gpu"] * args.gpus,
                            "per_gpu_batch": w["batch_per_gpu"], "parallelism": f"dp{args.gpus}"},
-                "cpu_baseline": {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": kind,
+                "cpu_baseline": {"value": round(ips, 3), "unit": w["unit"], "cores": cores, "kind": kind,
                                  "sample": f"each step is {sample} images of the batch through the reference's "
                                            f"kernels compiled for the host (OpenMP over work-items)"},
-                "e2e": {"value": round(ips, 3), "unit": "images/s", "h2d_bytes_per_step": 0,
+                "e2e": {"value": round(ips, 3), "unit": w["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0

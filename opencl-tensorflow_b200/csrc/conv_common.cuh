@@ -56,4 +56,12 @@ inline int check_int32_sizes(const ConvGeom& g) {
   return B2_OK;
 }
 
+// Narrow-filter Conv2D on the CUDA cores (conv_direct.cu): eligible when
+// Ci, Co <= 32 and kH*kW*Ci*Co <= 4608.  Callers have checked the shapes and
+// the 2^31-element limits.
+bool conv_direct_ok(const ConvGeom& g);
+int conv_direct_forward(const ConvGeom& g, const float* x, const float* w, float* y, cudaStream_t s);
+int conv_direct_backprop_input(const ConvGeom& g, const float* dy, const float* w, float* dx, cudaStream_t s);
+int conv_direct_backprop_filter(const ConvGeom& g, const float* x, const float* dy, float* dw, cudaStream_t s);
+
 }  // namespace b2

@@ -688,6 +688,7 @@ int b2_conv2d(b2_stream_t stream, const float* input, const int64_t input_shape[
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t M = g.N * g.Ho * g.Wo, K = g.kH * g.kW * g.Ci;
   if (M == 0 || g.Co == 0) return B2_OK;
+  if (conv_direct_ok(g)) return conv_direct_forward(g, input, filter, output, s);
   const MNMajor bv{filter, g.Co, g.Co};
   if (is_pointwise(g)) {
     const KContig av{input, M, g.Ci, aligned16(input) && g.Ci % 4 == 0};
@@ -721,6 +722,7 @@ int b2_conv2d_backprop_input(b2_stream_t stream, const int32_t input_sizes[4], c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t M = g.N * g.H * g.W, K = g.kH * g.kW * g.Co;
   if (M == 0 || g.Ci == 0) return B2_OK;
+  if (conv_direct_ok(g)) return conv_direct_backprop_input(g, out_backprop, filter, output, s);
   if (is_pointwise(g)) {
     const KContig av{out_backprop, M, g.Co, aligned16(out_backprop) && g.Co % 4 == 0};
     const KContig bv{filter, g.Ci, g.Co, aligned16(filter) && g.Co % 4 == 0};
@@ -751,6 +753,7 @@ int b2_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int6
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t M = g.kH * g.kW * g.Ci, K = g.N * g.Ho * g.Wo;
   if (M == 0 || g.Co == 0) return B2_OK;
+  if (conv_direct_ok(g)) return conv_direct_backprop_filter(g, input, out_backprop, output, s);
   const MNMajor bv{out_backprop, g.Co, g.Co};
   if (is_pointwise(g)) {
     const MNMajor av{input, g.Ci, g.Ci};
