@@ -67,6 +67,7 @@ def test_upsampling_1x_is_identity(otf):
                                         ((1, 1, 1, 5), (3, 4)), ((2, 4, 6, 8), (4, 2)), ((256, 4, 4, 8), (2, 2)),
                                         ((3, 7, 5, 6), (3, 3)),
                                         # images over 48 KB of dy take the global-memory gather
+                                        ((2, 18, 12, 16), (2, 2)), ((1, 25, 25, 9), (2, 2)),
                                         ((2, 40, 40, 8), (2, 2)), ((1, 33, 30, 5), (3, 2))])
 def test_upsampling_grad_matches_single_thread_reference(otf, port1, shape, size):
     rng = np.random.default_rng(3)
