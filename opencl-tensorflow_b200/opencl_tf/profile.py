@@ -172,13 +172,14 @@ def summarize(rows) -> dict:
 
 
 def _cli() -> int:
-    """Replay one op of the README network's training step, e.g. for ncu:
+    """Replay one op of a network's training step, e.g. for ncu:
 
         PYTHONPATH=opencl-tensorflow_b200 python -m opencl_tf.profile --op conv2d --call 0 --reps 3
 
-    records one step at --batch (default 256), then runs the --call-th call of
-    --op (in step order) --reps times after one warm-up run; --list prints
-    the step's op calls with their per-op times.
+    records one step of --model (build_model, the default, or uwb_loc_v3) at
+    --batch (default 256), then runs the --call-th call of --op (in step
+    order) --reps times after one warm-up run; --list prints the step's op
+    calls with their per-op times.
     """
     import argparse
     import sys
@@ -189,15 +190,21 @@ def _cli() -> int:
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--list", action="store_true")
+    ap.add_argument("--model", choices=["build_model", "uwb_loc_v3"], default="build_model")
     a = ap.parse_args()
-    from .model import build_model
+    from .model import build_model, build_uwb_loc_v3
     from .train import mse
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
-    model = build_model(device=dev)
     g = torch.Generator(device=dev).manual_seed(1)
-    x = torch.rand(a.batch, 64, 64, 3, device=dev, generator=g)
-    t = torch.rand(a.batch, 8, 8, 8, device=dev, generator=g)
+    if a.model == "uwb_loc_v3":
+        model = build_uwb_loc_v3(device=dev)
+        x = torch.randn(a.batch, 8, 6, 3, 16, 2, device=dev, generator=g)
+        t = torch.rand(a.batch, 36, 24, 1, device=dev, generator=g)
+    else:
+        model = build_model(device=dev)
+        x = torch.rand(a.batch, 64, 64, 3, device=dev, generator=g)
+        t = torch.rand(a.batch, 8, 8, 8, device=dev, generator=g)
     _, log = record_step(lambda: mse(model(x, training=True), t).backward())
     if a.list:
         for r, (name, *_rest) in zip(time_ops(log), log):
