@@ -287,16 +287,20 @@ __global__ void bn_inv_std_kernel(const float* __restrict__ var, int C, float ep
 
 // Elementwise passes are row-tiled like the reductions: thread
 // (cg_local, r_off) of CTA (row block, channel chunk) owns channels
-// c0 .. c0+VEC-1 and rows r_off, r_off + rpi, ... of its row block, so its
-// per-channel constants sit in registers and each row costs one vector load
-// per input and one vector store, four rows in flight per thread.
+// c0 .. c0+VEC-1 and every rpi-th row of its share, so its per-channel
+// constants sit in registers and each row costs one vector load per input and
+// one vector store, four rows in flight per thread.  The rows are split into
+// the same `ranges` as the preceding reduction pass (gridDim.x = ranges * S,
+// S CTAs interleaved on a range) and walked from the end of each range
+// backwards: the reduction walked its ranges forwards, so the rows it read
+// last, still in L2, are read first.
 struct RowTile {
   int c0;
-  int64_t r, r_end, step;
+  int64_t r, first, step;  // rows r, r - step, ... >= first
   bool active;
 };
 
-__device__ __forceinline__ RowTile row_tile(int64_t rows, const ChunkGeom& geo) {
+__device__ __forceinline__ RowTile row_tile(int64_t rows, const ChunkGeom& geo, int ranges) {
   RowTile rt;
   const int t = threadIdx.x;
   const int cg_local = t % geo.cg;
@@ -304,11 +308,14 @@ __device__ __forceinline__ RowTile row_tile(int64_t rows, const ChunkGeom& geo) 
   const int group = blockIdx.y * geo.cg + cg_local;
   rt.active = r_off < geo.rpi && group < geo.groups;
   rt.c0 = group * geo.vec;
-  const int64_t per_block = ceil_div(rows, gridDim.x);
-  const int64_t r_begin = (int64_t)blockIdx.x * per_block;
-  rt.r_end = r_begin + per_block < rows ? r_begin + per_block : rows;
-  rt.r = r_begin + r_off;
-  rt.step = geo.rpi;
+  const int S = gridDim.x / ranges;
+  const int range = blockIdx.x / S, sub = blockIdx.x % S;
+  const int64_t per_range = ceil_div(rows, ranges);
+  const int64_t r_begin = (int64_t)range * per_range;
+  const int64_t r_end = r_begin + per_range < rows ? r_begin + per_range : rows;
+  rt.step = (int64_t)geo.rpi * S;
+  rt.first = r_begin + r_off + (int64_t)sub * geo.rpi;
+  rt.r = rt.first < r_end ? rt.first + (r_end - 1 - rt.first) / rt.step * rt.step : rt.first - rt.step;
   return rt;
 }
 
@@ -318,9 +325,10 @@ template <int VEC, bool RELU>
 __global__ void __launch_bounds__(kThreads)
     bn_normalize_kernel(const float* __restrict__ x, const float* __restrict__ mean,
                         const float* __restrict__ inv_std, const float* __restrict__ gamma,
-                        const float* __restrict__ beta, float* __restrict__ y, int64_t rows, int C, ChunkGeom geo) {
+                        const float* __restrict__ beta, float* __restrict__ y, int64_t rows, int C, ChunkGeom geo,
+                        int ranges) {
   using V = typename VecT<VEC>::T;
-  RowTile rt = row_tile(rows, geo);
+  RowTile rt = row_tile(rows, geo, ranges);
   if (!rt.active) return;
   float m[VEC], iv[VEC], g[VEC], b[VEC];
 #pragma unroll
@@ -338,17 +346,17 @@ __global__ void __launch_bounds__(kThreads)
     }
   };
   constexpr int U = 4;
-  for (; rt.r + (U - 1) * rt.step < rt.r_end; rt.r += U * rt.step) {
+  for (; rt.r - (U - 1) * rt.step >= rt.first; rt.r -= U * rt.step) {
     float v[U][VEC], o[U][VEC];
 #pragma unroll
-    for (int u = 0; u < U; ++u) VecT<VEC>::to(*reinterpret_cast<const V*>(x + (rt.r + u * rt.step) * C + rt.c0), v[u]);
+    for (int u = 0; u < U; ++u) VecT<VEC>::to(*reinterpret_cast<const V*>(x + (rt.r - u * rt.step) * C + rt.c0), v[u]);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       one(v[u], o[u]);
-      VecT<VEC>::from(o[u], reinterpret_cast<V*>(y + (rt.r + u * rt.step) * C + rt.c0));
+      VecT<VEC>::from(o[u], reinterpret_cast<V*>(y + (rt.r - u * rt.step) * C + rt.c0));
     }
   }
-  for (; rt.r < rt.r_end; rt.r += rt.step) {
+  for (; rt.r >= rt.first; rt.r -= rt.step) {
     float v[VEC], o[VEC];
     VecT<VEC>::to(*reinterpret_cast<const V*>(x + rt.r * C + rt.c0), v);
     one(v, o);
@@ -381,10 +389,10 @@ __global__ void __launch_bounds__(kThreads)
     bn_grad_dx_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
                       const float* __restrict__ inv_std, const float* __restrict__ k1,
                       const float* __restrict__ grad_beta, const float* __restrict__ grad_gamma,
-                      float* __restrict__ dx, int64_t rows, int C, float nhw_f, ChunkGeom geo,
+                      float* __restrict__ dx, int64_t rows, int C, float nhw_f, ChunkGeom geo, int ranges,
                       const float* __restrict__ gamma = nullptr, const float* __restrict__ beta = nullptr) {
   using V = typename VecT<VEC>::T;
-  RowTile rt = row_tile(rows, geo);
+  RowTile rt = row_tile(rows, geo, ranges);
   if (!rt.active) return;
   float m[VEC], iv[VEC], kk[VEC], db[VEC], dg[VEC], gm[VEC], bt[VEC];
 #pragma unroll
@@ -409,21 +417,21 @@ __global__ void __launch_bounds__(kThreads)
     }
   };
   constexpr int U = 4;
-  for (; rt.r + (U - 1) * rt.step < rt.r_end; rt.r += U * rt.step) {
+  for (; rt.r - (U - 1) * rt.step >= rt.first; rt.r -= U * rt.step) {
     float vx[U][VEC], vg[U][VEC], o[VEC];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t off = (rt.r + u * rt.step) * C + rt.c0;
+      const int64_t off = (rt.r - u * rt.step) * C + rt.c0;
       VecT<VEC>::to(*reinterpret_cast<const V*>(x + off), vx[u]);
       VecT<VEC>::to(*reinterpret_cast<const V*>(dy + off), vg[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       one(vx[u], vg[u], o);
-      VecT<VEC>::from(o, reinterpret_cast<V*>(dx + (rt.r + u * rt.step) * C + rt.c0));
+      VecT<VEC>::from(o, reinterpret_cast<V*>(dx + (rt.r - u * rt.step) * C + rt.c0));
     }
   }
-  for (; rt.r < rt.r_end; rt.r += rt.step) {
+  for (; rt.r >= rt.first; rt.r -= rt.step) {
     float vx[VEC], vg[VEC], o[VEC];
     const int64_t off = rt.r * C + rt.c0;
     VecT<VEC>::to(*reinterpret_cast<const V*>(x + off), vx);
@@ -441,6 +449,20 @@ int ew_row_blocks(int64_t rows, const ChunkGeom& geo, int sm_count) {
   int64_t cap = ceil_div(rows, (int64_t)geo.rpi * 4);
   if (cap < 1) cap = 1;
   return (int)(want < cap ? want : cap);
+}
+
+// Row CTAs of an elementwise pass that follows a reduction over `ranges` row
+// blocks (0: none): `ranges` times the CTAs per range that keep about 8 CTAs
+// per SM.  Sets *ranges_out to the ranges the kernel splits the rows into.
+int ew_grid_x(int64_t rows, const ChunkGeom& geo, int sm_count, int ranges, int* ranges_out) {
+  const int ew = ew_row_blocks(rows, geo, sm_count);
+  if (ranges <= 0) {
+    *ranges_out = ew;
+    return ew;
+  }
+  const int per = ew / ranges > 1 ? ew / ranges : 1;
+  *ranges_out = ranges;
+  return ranges * per;
 }
 
 int validate_nhwc(const int64_t* s, const char* what) {
@@ -477,18 +499,20 @@ int launch_partials(cudaStream_t s, int mode, const float* x, const float* dy, c
 }
 
 int launch_normalize(cudaStream_t s, const float* x, const float* mean, const float* inv, const float* gamma,
-                     const float* beta, float* y, int64_t total, int C, bool vec_ok, bool relu = false) {
+                     const float* beta, float* y, int64_t total, int C, bool vec_ok, bool relu = false,
+                     int ranges = 0) {
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
   const ChunkGeom geo = chunk_geom(C, vec_ok);
   const int64_t rows = total / C;
-  dim3 grid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
+  int rg = 0;
+  dim3 grid(ew_grid_x(rows, geo, d->sm_count, ranges, &rg), geo.chunks);
   if (vec_ok) {
-    if (relu) bn_normalize_kernel<4, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
-    else bn_normalize_kernel<4, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+    if (relu) bn_normalize_kernel<4, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo, rg);
+    else bn_normalize_kernel<4, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo, rg);
   } else {
-    if (relu) bn_normalize_kernel<1, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
-    else bn_normalize_kernel<1, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo);
+    if (relu) bn_normalize_kernel<1, true><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo, rg);
+    else bn_normalize_kernel<1, false><<<grid, kThreads, 0, s>>>(x, mean, inv, gamma, beta, y, rows, C, geo, rg);
   }
   return check_launch(s, "bn_normalize");
 }
@@ -520,7 +544,8 @@ int bn_training(cudaStream_t s, const float* x, const int64_t* x_shape, const fl
                                                                 moving_mean, moving_var, momentum, one_minus_momentum);
   B2_RETURN_IF_ERROR(check_launch(s, "bn_stats_finalize"));
   if (total == 0) return B2_OK;
-  return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok, relu);
+  return launch_normalize(s, x, saved_mean, inv.as<float>(), gamma, beta, y, total, (int)C, vec_ok, relu,
+                          used_blocks);
 }
 
 // Backward: dx, dgamma, dbeta from dy (relu: dy = (y > 0 ? dz : 0) with y
@@ -555,21 +580,22 @@ int bn_grad(cudaStream_t s, const float* grad_y, const int64_t* grad_y_shape, co
   B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
   if (total == 0) return B2_OK;
   const float nhw_f = (float)(int)rows;
-  dim3 egrid(ew_row_blocks(rows, geo, d->sm_count), geo.chunks);
+  int rg = 0;
+  dim3 egrid(ew_grid_x(rows, geo, d->sm_count, used_blocks, &rg), geo.chunks);
   if (vec_ok) {
     if (relu)
       bn_grad_dx_kernel<4, true><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
-                                                           grad_x, rows, (int)C, nhw_f, geo, gamma, beta);
+                                                           grad_x, rows, (int)C, nhw_f, geo, rg, gamma, beta);
     else
       bn_grad_dx_kernel<4, false><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
-                                                            grad_x, rows, (int)C, nhw_f, geo);
+                                                            grad_x, rows, (int)C, nhw_f, geo, rg);
   } else {
     if (relu)
       bn_grad_dx_kernel<1, true><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
-                                                           grad_x, rows, (int)C, nhw_f, geo, gamma, beta);
+                                                           grad_x, rows, (int)C, nhw_f, geo, rg, gamma, beta);
     else
       bn_grad_dx_kernel<1, false><<<egrid, kThreads, 0, s>>>(grad_y, x, saved_mean, inv, k1, grad_beta, grad_gamma,
-                                                            grad_x, rows, (int)C, nhw_f, geo);
+                                                            grad_x, rows, (int)C, nhw_f, geo, rg);
   }
   return check_launch(s, "bn_backward_dx");
 }
