@@ -349,6 +349,17 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     loss_value = float(loss_host)
 
+    # the batch's host->device copy alone (copy stream, events), for reading e2e
+    h_s, h_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(copy_stream):
+        h_s.record(copy_stream)
+        for _ in range(5):
+            stage_x[0].copy_(x_host, non_blocking=True)
+            stage_t[0].copy_(t_host, non_blocking=True)
+        h_e.record(copy_stream)
+    torch.cuda.synchronize(dev)
+    h2d_ms = h_s.elapsed_time(h_e) / 5
+
     # ---- per-op table and the dominant op's roofline (rank 0, outside the timed regions)
     per_op, roof = None, None
     if rank == 0:
@@ -387,6 +398,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(images / (ms_e2e * 1e-3), 2), "unit": w["unit"],
                 "h2d_bytes_per_step": int(x_host.numel() * 4 + t_host.numel() * 4), "d2h_bytes_per_step": 4,
                 "ms_per_step": round(ms_e2e / args.steps, 4),
+                "h2d_ms_alone": round(h2d_ms, 4),
                 "pipeline": "next batch copied host->device on a copy stream during the step; each step's "
                             "events enclose that copy and the loss read-back"},
         "gpu_launches": int(per_step_launches * args.steps),
