@@ -1,4 +1,4 @@
-"""The BASELINE configurations at full size.
+"""The benchmark workloads of the hot path at full size.
 
 c1  Conv2D fwd + dL/dx + dL/dw: x [8,64,64,3] ~N(0,1), w [3,7,3,48] He-normal,
     strides (1,1,2,1) SAME, upstream grad [8,64,32,48] ~N(0,1).
