@@ -192,15 +192,20 @@ int b2_batch_norm_training(b2_stream_t stream, const float* x,
                            int64_t beta_len, float epsilon, float* y,
                            float* saved_mean, float* saved_var);
 
-/* Same computation and outputs as b2_batch_norm_training, for callers that
- * must not have device memory allocated during a call -- a runtime whose
- * memory manager owns all of HBM, or a warm serving loop that cannot accept
- * an allocation's synchronisation and latency.  It has no counterpart in the
- * reference.  Its reduction scratch is a fixed 256 KiB array in the library's
- * device image (held on every GPU that loads the library until exit), so it
- * accepts at most 16384 channels and returns B2_ERR_INVALID_ARGUMENT beyond
- * that.  The first call on each device looks up that array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+/* The computation of b2_batch_norm_training, for callers that must not
+ * have device memory allocated during a call -- a runtime whose memory
+ * manager owns all of HBM, or a warm serving loop that cannot accept an
+ * allocation's synchronisation and latency.  It has no counterpart in the
+ * reference.  Its outputs equal b2_batch_norm_training's within the fp32
+ * tolerance; they are bit-identical only while C <= 55: for more channels
+ * the statistics are summed over fewer row-block partials (so that they fit
+ * the fixed array below), which changes the order of the additions.  Its
+ * reduction scratch is a fixed 256 KiB array in the library's device image
+ * (held on every GPU that loads the library until exit), so it accepts at
+ * most 16384 channels and returns B2_ERR_INVALID_ARGUMENT beyond that.  The
+ * first call on each device looks up that array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture (a
+ * failed lookup is retried by the next call).
  * All calls on a device share the array: calls whose work overlaps on the GPU
  * (different streams, no ordering between them) race and corrupt each
  * other's statistics, so order them (e.g. issue them on one stream). */
@@ -369,6 +374,24 @@ int b2_adam_update(b2_stream_t stream, int num_tensors, float* const* params,
  * expired since the library was loaded; synchronise the stream first.  A
  * nonzero count means a kernel gave up waiting and its output is invalid. */
 int b2_device_timeouts(unsigned int* count);
+
+/* ---- Device-side wait failures as op errors ------------------------------
+ * The reference turns every device failure into a TF status
+ * (OP_REQUIRES_CL -> errors::Internal, src/ops/conv2d_ops.cc:43-45).  Here
+ * the ops are asynchronous, so a kernel whose bounded wait expired (its
+ * pipeline then tears down cleanly and the context stays usable) records the
+ * expiry in host-mapped memory, and:
+ *   - every op call made once the expiry is visible returns B2_ERR_TIMEOUT
+ *     (the work is still enqueued; its results are invalid), until
+ *   - b2_stream_status(stream), which synchronises `stream`, returns
+ *     B2_ERR_TIMEOUT once for the expiry and clears it (else B2_OK).
+ * The state is process-wide (all devices and streams). */
+int b2_stream_status(b2_stream_t stream);
+
+/* Limit of each bounded device-side wait, in nanoseconds, for kernels
+ * launched after the call; 0 restores the default (10 s).  A test hook: a
+ * very short limit makes a real pipeline's waits run out. */
+int b2_set_wait_limit_ns(uint64_t limit_ns);
 
 #ifdef __cplusplus
 }

@@ -6,8 +6,10 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 
 #include "b2_opencl_tf.h"
 
@@ -42,8 +44,39 @@ void clear_error();
 
 // Checks the last launch; with B2_DEBUG_CHECKS=1 in the environment it also
 // synchronises the stream (outside graph capture) so a device fault is
-// attributed to the op that caused it.
+// attributed to the op that caused it.  Returns B2_ERR_TIMEOUT while an
+// expired device-side wait is pending (see WaitParams).
 int check_launch(cudaStream_t s, const char* what);
+
+// ------------------------------------------------------- bounded waits
+
+// Every spin-wait in this library's kernels (the mbarrier waits of the
+// tensor-core pipelines and of the staged depthwise filter gradient) gives up
+// after limit_ns.  The kernel then counts the expiry on the device, stores 1
+// into `expired` -- a word of host-mapped memory -- and tears its pipeline
+// down cleanly (in-flight copies land, TMEM is freed).  check_launch() reads
+// that word without synchronising, so every call made after the expiry became
+// visible fails with B2_ERR_TIMEOUT until b2_stream_status() clears it.
+struct WaitParams {
+  uint64_t limit_ns;
+  unsigned int* expired;  // host-mapped, device-visible; null if unavailable
+};
+
+constexpr uint64_t kDefaultWaitLimitNs = 10ull * 1000 * 1000 * 1000;  // 10 s
+
+// The limit set by b2_set_wait_limit_ns (default 10 s) and the flag word.
+WaitParams wait_params();
+
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at
+// least `need` bytes before its first launch there.  The attribute belongs to the
+// device's context, so it is tracked per device; concurrent first calls from
+// several host threads are serialised.
+struct SmemOptIn {
+  static constexpr int kDevices = 64;
+  std::atomic<int> bytes[kDevices] = {};
+  std::mutex mu;
+  int ensure(const void* kernel, int device, int need);
+};
 
 // ------------------------------------------------------------ device state
 

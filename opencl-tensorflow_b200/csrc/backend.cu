@@ -29,6 +29,35 @@ std::string g_device_error[kMaxDevices];
 std::atomic<uint64_t> g_num_allocs[kMaxDevices];
 std::atomic<uint64_t> g_launches{0};
 
+// Bounded device-side waits: the limit kernels are launched with, and the
+// host-mapped word they set when a wait expires (allocated with the first
+// device's state, before any stream capture can be in progress).
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
+std::once_flag g_expired_once;
+unsigned int* g_expired_host = nullptr;  // host view
+unsigned int* g_expired_dev = nullptr;   // device view of the same word
+
+void alloc_expired_flag() {
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, sizeof(unsigned int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFreeHost(h);
+    return;
+  }
+  *static_cast<volatile unsigned int*>(h) = 0u;
+  g_expired_host = static_cast<unsigned int*>(h);
+  g_expired_dev = static_cast<unsigned int*>(d);
+}
+
+bool wait_expired() {
+  return g_expired_host != nullptr && *static_cast<volatile unsigned int*>(g_expired_host) != 0u;
+}
+
 bool env_flag(const char* name) {
   const char* v = std::getenv(name);
   return v != nullptr && v[0] != '\0' && std::strcmp(v, "0") != 0;
@@ -79,6 +108,7 @@ void init_device(int dev) {
       cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
     }
   }
+  if (st == B2_OK) std::call_once(g_expired_once, alloc_expired_flag);
   g_device_status[dev] = st;
   g_device_error[dev] = err;
 }
@@ -125,6 +155,26 @@ int check_launch(cudaStream_t s, const char* what) {
                          cudaGetErrorString(e));
     }
   }
+  if (wait_expired())
+    return set_error(B2_ERR_TIMEOUT,
+                     "a bounded device-side wait of an earlier kernel of this library expired (checked after "
+                     "launching %s); results since then are invalid until b2_stream_status() reports and "
+                     "clears it", what);
+  return B2_OK;
+}
+
+WaitParams wait_params() {
+  return WaitParams{g_wait_limit_ns.load(std::memory_order_relaxed), g_expired_dev};
+}
+
+int SmemOptIn::ensure(const void* kernel, int device, int need) {
+  if (device < 0 || device >= kDevices)
+    return set_error(B2_ERR_NO_DEVICE, "device ordinal %d out of range", device);
+  if (bytes[device].load(std::memory_order_acquire) >= need) return B2_OK;
+  std::lock_guard<std::mutex> lock(mu);
+  if (bytes[device].load(std::memory_order_relaxed) >= need) return B2_OK;
+  B2_CUDA_OR_RETURN(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, need));
+  bytes[device].store(need, std::memory_order_release);
   return B2_OK;
 }
 
@@ -237,6 +287,26 @@ int b2_pool_stats(b2_pool_stats_t* out) {
 
 int b2_kernel_launch_count(uint64_t* count) {
   *count = g_launches.load(std::memory_order_relaxed);
+  return B2_OK;
+}
+
+int b2_set_wait_limit_ns(uint64_t limit_ns) {
+  clear_error();
+  g_wait_limit_ns.store(limit_ns == 0 ? kDefaultWaitLimitNs : limit_ns, std::memory_order_relaxed);
+  return B2_OK;
+}
+
+int b2_stream_status(b2_stream_t stream) {
+  clear_error();
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  B2_CUDA_OR_RETURN(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  if (wait_expired()) {
+    *static_cast<volatile unsigned int*>(g_expired_host) = 0u;
+    return set_error(B2_ERR_TIMEOUT,
+                     "a bounded device-side wait expired: the kernel gave up, so the outputs of the calls "
+                     "enqueued before this check are invalid (state cleared)");
+  }
   return B2_OK;
 }
 

@@ -18,6 +18,7 @@
 // reference formulas with round-to-nearest intrinsics (no contraction) and
 // inv_std = 1/sqrt(var+eps) in IEEE fp32, so, given the same statistics,
 // y and grad_x are bit-identical to the reference's formula.
+#include <atomic>
 #include <mutex>
 
 #include "b2_internal.cuh"
@@ -719,13 +720,28 @@ constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) float2 g_bn_no_alloc_scratch[kNoAllocScratch];
 
 namespace {
-std::once_flag g_no_alloc_once[kNoAllocMaxDevices];
-void* g_no_alloc_addr[kNoAllocMaxDevices];
-cudaError_t g_no_alloc_status[kNoAllocMaxDevices];
+std::mutex g_no_alloc_mu;
+std::atomic<void*> g_no_alloc_addr[kNoAllocMaxDevices];
 
-// Runs once per device, with that device current.
-void resolve_no_alloc_scratch(int dev) {
-  g_no_alloc_status[dev] = cudaGetSymbolAddress(&g_no_alloc_addr[dev], g_bn_no_alloc_scratch);
+// The array's device address on `dev` (the current device), looked up on the
+// first call there.  Only a successful lookup is kept: a lookup that failed
+// (for instance one attempted while a stream was being captured) is retried
+// by the next call instead of failing every later call.
+cudaError_t no_alloc_scratch(int dev, void** addr) {
+  *addr = g_no_alloc_addr[dev].load(std::memory_order_acquire);
+  if (*addr) return cudaSuccess;
+  std::lock_guard<std::mutex> lock(g_no_alloc_mu);
+  *addr = g_no_alloc_addr[dev].load(std::memory_order_relaxed);
+  if (*addr) return cudaSuccess;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_bn_no_alloc_scratch);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not sticky: clear it so the next call can retry
+    return e;
+  }
+  g_no_alloc_addr[dev].store(p, std::memory_order_release);
+  *addr = p;
+  return cudaSuccess;
 }
 }  // namespace
 
@@ -748,10 +764,11 @@ extern "C" int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* 
   B2_RETURN_IF_ERROR(device_info(&d));
   const int dev = d->device;
   B2_REQUIRE(dev < kNoAllocMaxDevices, "device ordinal %d out of range", dev);
-  std::call_once(g_no_alloc_once[dev], resolve_no_alloc_scratch, dev);
-  if (g_no_alloc_status[dev] != cudaSuccess)
+  void* scratch = nullptr;
+  const cudaError_t se = no_alloc_scratch(dev, &scratch);
+  if (se != cudaSuccess)
     return set_error(B2_ERR_INTERNAL, "cudaGetSymbolAddress of the static scratch failed (cuda_err=%d: %s)",
-                     (int)g_no_alloc_status[dev], cudaGetErrorString(g_no_alloc_status[dev]));
+                     (int)se, cudaGetErrorString(se));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(y);
   const ChunkGeom geo = chunk_geom(C, vec_ok);
@@ -759,7 +776,7 @@ extern "C" int b2_batch_norm_training_no_alloc(b2_stream_t stream, const float* 
   const int64_t fit = (kNoAllocScratch - ceil_div(C, 2)) / C;
   int blocks = row_blocks(rows, geo.chunks, d->sm_count);
   if (blocks > fit) blocks = (int)fit;
-  float2* partial = static_cast<float2*>(g_no_alloc_addr[dev]);
+  float2* partial = static_cast<float2*>(scratch);
   float* inv = reinterpret_cast<float*>(partial + (int64_t)blocks * C);
   // Every scratch entry read below is written earlier in this call, so no
   // clearing is needed; the previous call's contents are simply overwritten.

@@ -445,15 +445,21 @@ __device__ __forceinline__ bool bar_try_wait(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for the phase of parity `parity`, at most 10 s; a timeout is counted.
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+// Wait for the phase of parity `parity`, at most limit_ns; an expiry is
+// counted and set in the library's host-mapped expiry word (so the op calls
+// that follow return B2_ERR_TIMEOUT).
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, uint64_t limit_ns, unsigned int* expired) {
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   while (!bar_try_wait(b, parity)) {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > 10ull * 1000 * 1000 * 1000) {
+    if (t - t0 > limit_ns) {
       atomicAdd(&g_dw_timeouts, 1u);
+      if (expired) {
+        *reinterpret_cast<volatile unsigned int*>(expired) = 1u;
+        __threadfence_system();
+      }
       return false;
     }
   }
@@ -472,6 +478,7 @@ struct DwStage {
   int padL;        // zero pixels staged before each input row
   int Wp;          // staged input row width (pixels)
   int slot_floats; // Wo*C + kH*Wp*C
+  WaitParams wait; // limit of the pipeline waits, expiry word
 };
 
 constexpr int kStagedConsumers = 256;  // consumer threads of a staged CTA (one producer warp on top)
@@ -531,7 +538,8 @@ __global__ void __launch_bounds__(32 + kStagedConsumers) dw_wgrad_staged_kernel(
       int issued = 0;
       for (int i = 0; i < nr; ++i, ++issued) {
         const int sl = i % st.slots;
-        if (i >= st.slots && !bar_wait(&empty[sl], (uint32_t)(i / st.slots - 1) & 1u)) break;
+        if (i >= st.slots && !bar_wait(&empty[sl], (uint32_t)(i / st.slots - 1) & 1u, st.wait.limit_ns, st.wait.expired))
+          break;
         const int r = r0 + i;
         const int n = r / a.Ho, ho = r - n * a.Ho;
         float* base = slots + (size_t)sl * st.slot_floats;
@@ -553,12 +561,13 @@ __global__ void __launch_bounds__(32 + kStagedConsumers) dw_wgrad_staged_kernel(
       }
       // let every issued copy land before the CTA can exit
       const int first = issued > st.slots ? issued - st.slots : 0;
-      for (int i = first; i < issued; ++i) bar_wait(&full[i % st.slots], (uint32_t)(i / st.slots) & 1u);
+      for (int i = first; i < issued; ++i)
+        bar_wait(&full[i % st.slots], (uint32_t)(i / st.slots) & 1u, kDefaultWaitLimitNs, st.wait.expired);
     }
   } else if (ct < consumer_warps * 32) {
     for (int i = 0; i < nr; ++i) {
       const int sl = i % st.slots;
-      if (!bar_wait(&full[sl], (uint32_t)(i / st.slots) & 1u)) break;
+      if (!bar_wait(&full[sl], (uint32_t)(i / st.slots) & 1u, st.wait.limit_ns, st.wait.expired)) break;
       const float* base = slots + (size_t)sl * st.slot_floats;
       if (active && KMAX == 9 && a.kH == 3 && a.kW == 3) {
         // 3x3: tap offsets fixed at compile time, row validity read once per row
@@ -855,14 +864,11 @@ int b2_depthwise_conv2d_backprop_filter(b2_stream_t stream, const float* input, 
   const int64_t slot_floats = g.Wo * g.Ci + g.kH * Wp * g.Ci;
   const int64_t slots = slot_floats > 0 ? (int64_t)100 * 1024 / (slot_floats * 4) : 0;
   if (vec && slots >= 2 && g.Ci / 4 <= kStagedConsumers && g.N * g.Ho <= kMaxInt32) {
-    const DwStage st{(int)(slots > 6 ? 6 : slots), (int)padL, (int)Wp, (int)slot_floats};
+    const DwStage st{(int)(slots > 6 ? 6 : slots), (int)padL, (int)Wp, (int)slot_floats, wait_params()};
     const size_t smem = (size_t)st.slots * st.slot_floats * 4 + 16 * st.slots + 4 * st.slots * g.kH + 16;
-    static bool configured = false;
-    if (!configured) {
-      B2_CUDA_OR_RETURN(cudaFuncSetAttribute(dw_wgrad_staged_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             110 * 1024));
-      configured = true;
-    }
+    static SmemOptIn opt_in;
+    B2_RETURN_IF_ERROR(
+        opt_in.ensure(reinterpret_cast<const void*>(dw_wgrad_staged_kernel<9>), d->device, 110 * 1024));
     const int cgx = (int)(g.Ci / 4);
     int lanes_y = kStagedConsumers / cgx;
     if (lanes_y > g.Wo) lanes_y = (int)g.Wo;

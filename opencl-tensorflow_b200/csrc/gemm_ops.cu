@@ -430,13 +430,14 @@ int launch_tma(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
                int raw_stages, int op_stages, int grid, cudaStream_t s, const char* name) {
   const TmaSmem plan = tma_smem_plan(prob.bn, raw_stages, op_stages, AK == kAFpropRows ? im_table_entries(prob.K) : 0,
                                      prob.b_res_kb);
-  static int configured_bytes = 0;  // per instantiation
-  if ((int)plan.total > configured_bytes) {
-    B2_CUDA_OR_RETURN(cudaFuncSetAttribute(tma_gemm_kernel<AK, kBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)plan.total));
-    configured_bytes = (int)plan.total;
-  }
-  tma_gemm_kernel<AK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, prob, raw_stages, op_stages);
+  const DeviceInfo* d = nullptr;
+  B2_RETURN_IF_ERROR(device_info(&d));
+  static SmemOptIn opt_in;  // per instantiation
+  B2_RETURN_IF_ERROR(
+      opt_in.ensure(reinterpret_cast<const void*>(tma_gemm_kernel<AK, kBK>), d->device, (int)plan.total));
+  TmaProblem p = prob;
+  p.wait = wait_params();
+  tma_gemm_kernel<AK, kBK><<<grid, kTmaThreads, plan.total, s>>>(ma, mb, md, p, raw_stages, op_stages);
   return check_launch(s, name);
 }
 

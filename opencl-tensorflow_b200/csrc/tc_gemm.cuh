@@ -40,9 +40,11 @@
 // 500k pixels, K = 4096 GEMMs) at fp32-class accuracy; tiles whose K fits in
 // one chunk go straight from P to global memory.
 //
-// Every mbarrier wait is bounded by a wall-clock limit; on expiry the thread
-// counts the event in g_tc_timeouts (read by b2_device_timeouts()) and the
-// CTA stops issuing work, still frees its TMEM and exits.
+// Every mbarrier wait is bounded by a wall-clock limit (a launch parameter);
+// on expiry the thread counts the event in g_tc_timeouts (read by
+// b2_device_timeouts()), sets the library's host-mapped expiry word (the op
+// calls that follow fail with B2_ERR_TIMEOUT) and the CTA stops issuing work,
+// waits for the MMAs it issued, frees its TMEM and exits.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -64,7 +66,7 @@ constexpr int kMaxStages = 6;
 constexpr int kUnit = 8;  // k elements per producer unit
 constexpr int kChunkKB = 8;  // k-blocks accumulated in one TMEM chunk (256 k)
 constexpr int kMaxBN = 160;  // three BN-column regions must fit in 512 TMEM columns
-constexpr uint64_t kWaitLimitNs = 10ull * 1000 * 1000 * 1000;  // 10 s
+constexpr uint64_t kWaitLimitNs = kDefaultWaitLimitNs;  // drain waits after an abort (fixed)
 
 // Count of bounded waits that expired, read by the host through
 // b2_device_timeouts() (internal linkage: one counter per translation unit
@@ -103,20 +105,61 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Bounded wait for the phase of parity `parity` on `bar`.  On expiry: count
-// the timeout, raise the CTA's abort flag and return false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Per-CTA state of the bounded waits, in shared memory: the abort flag the
+// first expired wait raises (every other wait of the CTA then gives up too),
+// the limit of one wait and the library's host-mapped expiry word.
+struct WaitState {
+  int abort;
+  uint64_t limit_ns;
+  unsigned int* expired;
+};
+
+// Thread 0 of the CTA, before the block-wide barrier that precedes any wait.
+__device__ __forceinline__ void wait_state_init(WaitState* ws, const WaitParams& wp) {
+  ws->abort = 0;
+  ws->limit_ns = wp.limit_ns;
+  ws->expired = wp.expired;
+}
+
+__device__ __forceinline__ bool aborted(const WaitState* ws) {
+  return *reinterpret_cast<const volatile int*>(&ws->abort) != 0;
+}
+
+// Record an expired wait: the device counter, the host-visible word.
+__device__ __forceinline__ void note_expiry(unsigned int* expired) {
+  atomicAdd(&g_tc_timeouts, 1u);
+  if (expired) {
+    *reinterpret_cast<volatile unsigned int*>(expired) = 1u;
+    __threadfence_system();
+  }
+}
+
+// Bounded wait for the phase of parity `parity` on `bar`.  On expiry: record
+// it, raise the CTA's abort flag and return false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, WaitState* ws) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        atomicAdd(&g_tc_timeouts, 1u);
-        *abort_flag = 1;
+    if ((it & 255u) == 0) {  // the clock and the abort flag: after the second failed try, then every 256
+      if (aborted(ws)) return false;
+      if (global_ns() - t0 > ws->limit_ns) {
+        note_expiry(ws->expired);
+        *reinterpret_cast<volatile int*>(&ws->abort) = 1;
         return false;
       }
+    }
+  }
+}
+
+// Wait bounded by the fixed drain limit only (used while tearing down after
+// an abort, for work already issued: copies in flight, MMAs issued).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, unsigned int* expired = nullptr) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      note_expiry(expired);
+      return;
     }
   }
 }
@@ -276,6 +319,7 @@ struct GemmProblem {
   int64_t k_per_split;  // multiple of BK
   int splits;
   Epilogue ep;
+  WaitParams wait;  // set by launch_gemm
 };
 
 struct KernelSmem {
@@ -292,7 +336,7 @@ inline KernelSmem smem_plan(int bn, int stages) {
   s.b_bytes = (size_t)bn * BK * 4;
   s.stage_bytes = 2 * s.a_bytes + 2 * s.b_bytes;
   s.bar_offset = s.stage_bytes * stages;
-  s.total = s.bar_offset + 8 * (2 * kMaxStages + 4) + 16 + 1024;  // + alignment slack
+  s.total = s.bar_offset + 8 * (2 * kMaxStages + 5) + 16 + 1024;  // + alignment slack
   return s;
 }
 
@@ -328,9 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
   uint64_t* empty = full + kMaxStages;
   uint64_t* chunk_full = empty + kMaxStages;  // [2]
   uint64_t* chunk_empty = chunk_full + 2;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(chunk_empty + 2);
-  __shared__ int s_abort;
-  volatile int* abort_flag = &s_abort;
+  uint64_t* mma_done = chunk_empty + 2;  // every MMA this CTA issued has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  __shared__ WaitState s_wait;
+  WaitState* ws = &s_wait;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -342,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
                              : need_cols <= 256 ? 256u : 512u;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    wait_state_init(ws, p.wait);
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], kProducerWarps * 32);
       mbar_init(&empty[s], 1);
@@ -351,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
       mbar_init(&chunk_full[a], 1);
       mbar_init(&chunk_empty[a], 128);
     }
+    mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kMmaWarp) {
@@ -370,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
     const int rsub = 8 * warp + (lane & 7);
     const int q = lane >> 3;
     uint32_t stage_cnt = 0;
-    for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+    for (int64_t t = blockIdx.x; t < tiles && !aborted(ws); t += gridDim.x) {
       const TileCoord tc = tile_coord(p, bn, t);
       const auto ca0 = p.a.row(tc.m0 + rsub);
       const auto ca1 = p.a.row(tc.m0 + rsub + 64);
@@ -394,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
             if (tc.n0 + r < p.N) p.b.load8(cb[j], k, tc.k_end, vb[j]); else zero_unit(vb[j]);
           }
         }
-        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, abort_flag)) break;
+        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, ws)) break;
         uint8_t* st = smem + (size_t)s * stage_bytes;
         store_unit_split(st, st + a_bytes, rsub, q, va0);
         store_unit_split(st, st + a_bytes, rsub + 64, q, va1);
@@ -415,12 +461,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
       const uint32_t idesc = idesc_tf32(bn);
       uint32_t stage_cnt = 0, g = 0;  // g counts chunks
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
+      for (int64_t t = blockIdx.x; t < tiles && ok && !aborted(ws); t += gridDim.x) {
         const TileCoord tc = tile_coord(p, bn, t);
         for (int kb0 = 0; kb0 < tc.nkb && ok; kb0 += kChunkKB, ++g) {
           const int a = (int)(g & 1u);
           const uint32_t use = g >> 1;
-          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, abort_flag)) {
+          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, ws)) {
             ok = false;
             break;
           }
@@ -429,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
           const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
           for (int kb = kb0; kb < kb1; ++kb, ++stage_cnt) {
             const int s = (int)(stage_cnt % (uint32_t)stages);
-            if (!mbar_wait(&full[s], (stage_cnt / (uint32_t)stages) & 1u, abort_flag)) {
+            if (!mbar_wait(&full[s], (stage_cnt / (uint32_t)stages) & 1u, ws)) {
               ok = false;
               break;
             }
@@ -449,6 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
           mma_commit(&chunk_full[a]);
         }
       }
+      // TMEM is freed at the end of the kernel: after an aborted pipeline the
+      // epilogue may not have waited for the last MMAs, so wait for them here
+      mma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, ws->expired);
     }
   } else {
     // ----------------------------------------------------------- epilogue
@@ -466,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const P p, const i
         const bool first = ch == 0, last = ch + 1 >= nch;
         const int a = (int)(g & 1u);
         if (nch > 0) {
-          if (!mbar_wait(&chunk_full[a], (g >> 1) & 1u, abort_flag)) {
+          if (!mbar_wait(&chunk_full[a], (g >> 1) & 1u, ws)) {
             ok = false;
             break;
           }
@@ -552,12 +602,9 @@ int launch_gemm(P prob, int bn, cudaStream_t s, const char* name) {
   B2_RETURN_IF_ERROR(device_info(&d));
   const int stages = choose_stages(bn, d->max_smem_optin);
   const KernelSmem plan = smem_plan(bn, stages);
-  static int configured_bytes = 0;  // per template instantiation
-  if ((int)plan.total > configured_bytes) {
-    B2_CUDA_OR_RETURN(
-        cudaFuncSetAttribute(tc_gemm_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.total));
-    configured_bytes = (int)plan.total;
-  }
+  static SmemOptIn opt_in;  // per template instantiation
+  B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(tc_gemm_kernel<P>), d->device, (int)plan.total));
+  prob.wait = wait_params();
   const int64_t tiles = ceil_div(prob.N, bn) * ceil_div(prob.M, BM) * prob.splits;
   const int grid = (int)(tiles < d->sm_count ? tiles : d->sm_count);
   tc_gemm_kernel<P><<<grid, kThreads, plan.total, s>>>(prob, bn, stages);

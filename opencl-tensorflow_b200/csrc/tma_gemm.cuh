@@ -54,9 +54,11 @@
 // long reductions fold every 256 k into S (round-to-nearest fp32 adds), as the
 // register-fed engine does.
 //
-// Every mbarrier wait is bounded; on expiry the CTA raises its abort flag,
-// lets TMA loads already issued land, waits for its own TMA stores, frees its
-// TMEM and exits, and the expiry is counted in g_tc_timeouts.
+// Every mbarrier wait is bounded (the limit is a launch parameter); on expiry
+// the CTA raises its abort flag, lets TMA loads already issued land, waits for
+// its own TMA stores and for the MMAs it issued, frees its TMEM and exits; the
+// expiry is counted in g_tc_timeouts and set in the host-mapped expiry word,
+// so the op calls that follow return B2_ERR_TIMEOUT.
 #pragma once
 
 #include <cuda.h>
@@ -134,6 +136,7 @@ struct TmaProblem {
                       // k-blocks, loaded and split once and kept in shared memory
   FastDiv nt_div, mt_div;  // N tiles, M tiles (tile indices < 2^31)
   FastDiv wo_div, ho_div, kwc_div;  // conv kinds: Wo, Ho and kW * Ci
+  WaitParams wait;                  // limit of each pipeline wait, expiry word
 };
 
 // TMEM columns used by the accumulators (P0, P1 and, when needed, S).
@@ -178,17 +181,6 @@ __host__ __device__ inline TmaSmem tma_smem_plan(int bn, int raw_stages, int op_
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
-}
-
-// Wait bounded by time only (used while draining, after an abort).
-__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) {
-      atomicAdd(&g_tc_timeouts, 1u);
-      return;
-    }
-  }
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -546,8 +538,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint64_t* b_ready = b_full + 1;                     // resident B split (one arrival per converter warp)
   uint64_t* mma_done = b_ready + 1;                   // every MMA this CTA issued has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  __shared__ int s_abort;
-  volatile int* abort_flag = &s_abort;
+  __shared__ WaitState s_wait;
+  WaitState* ws = &s_wait;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -564,7 +556,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint32_t it_iss = 0;
   TmaTile tc_iss{};
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    wait_state_init(ws, p.wait);
     for (int s = 0; s < raw_stages; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], 4);
@@ -626,7 +618,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (lane == 0) {
       uint32_t s = 0, lap = 1;  // it_iss = lap * R + s (it_iss == R here unless the work ran out)
       while (t_iss < tiles) {
-        if (!mbar_wait(&raw_empty[s], (lap - 1) & 1u, abort_flag)) break;
+        if (!mbar_wait(&raw_empty[s], (lap - 1) & 1u, ws)) break;
         issue_stage<AK, kBK>(&map_a, &map_b, smem_u32(smem + (size_t)s * plan.raw_bytes), plan.a_bytes,
                              &raw_full[s], tx, p, tc_iss, kb_iss);
         ++it_iss;
@@ -642,8 +634,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       }
       // Let every issued load land before the CTA can exit.
       const uint32_t n = it_iss < R ? it_iss : R;
-      for (uint32_t i = it_iss - n; i < it_iss; ++i) mbar_wait_drain(&raw_full[i % R], (i / R) & 1u);
-      if (bres && blockIdx.x < tiles) mbar_wait_drain(b_full, 0);
+      for (uint32_t i = it_iss - n; i < it_iss; ++i) mbar_wait_drain(&raw_full[i % R], (i / R) & 1u, ws->expired);
+      if (bres && blockIdx.x < tiles) mbar_wait_drain(b_full, 0, ws->expired);
     }
   } else if (warp >= kConvWarp0 && warp < kTmaEpiWarp0) {
     // ---------------------------------------------------------- converters
@@ -661,7 +653,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     bool ok = true;
     if (bres && blockIdx.x < tiles) {
       // split the resident B tile in place, all converter warps together
-      ok = mbar_wait(b_full, 0, abort_flag);
+      ok = mbar_wait(b_full, 0, ws);
       if (ok) {
         const int ct = (warp - kConvWarp0) * 32 + lane;
         const int words = p.b_res_kb * b_words;
@@ -694,7 +686,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         }
         if ((int)(i & 1u) != group) continue;
         const uint32_t sr = cur_sr, sq = cur_sq;
-        if (!mbar_wait(&raw_full[sr], cur_lr & 1u, abort_flag)) {
+        if (!mbar_wait(&raw_full[sr], cur_lr & 1u, ws)) {
           ok = false;
           break;
         }
@@ -714,7 +706,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             wb[j] = *reinterpret_cast<const uint4*>(raw + plan.a_bytes + 16 * (gt + j * kGroupThreads));
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[sr]);  // this warp has read the raw stage
-        if (cur_lq > 0 && !mbar_wait(&op_empty[sq], (cur_lq - 1) & 1u, abort_flag)) {
+        if (cur_lq > 0 && !mbar_wait(&op_empty[sq], (cur_lq - 1) & 1u, ws)) {
           ok = false;
           break;
         }
@@ -749,13 +741,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       const uint32_t idesc = idesc_tf32_major(bn, false, !kBK);
       uint32_t it = 0, g = 0;  // g counts chunks
       uint32_t sq = 0, lap_q = 0;  // it = lap_q * Q + sq
-      bool ok = !(bres && blockIdx.x < tiles) || mbar_wait(b_ready, 0, abort_flag);
-      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
+      bool ok = !(bres && blockIdx.x < tiles) || mbar_wait(b_ready, 0, ws);
+      for (int64_t t = blockIdx.x; t < tiles && ok && !aborted(ws); t += gridDim.x) {
         const TmaTile tc = tma_tile(p, t);
         for (int kb0 = 0; kb0 < tc.nkb && ok; kb0 += kChunkKB, ++g) {
           const int a = (int)(g & 1u);
           const uint32_t use = g >> 1;
-          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, abort_flag)) {
+          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, ws)) {
             ok = false;
             break;
           }
@@ -763,7 +755,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
           const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            if (!mbar_wait(&op_full[sq], lap_q & 1u, abort_flag)) {
+            if (!mbar_wait(&op_full[sq], lap_q & 1u, ws)) {
               ok = false;
               break;
             }
@@ -789,7 +781,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       // TMEM is freed at the end of the kernel: after an aborted pipeline the
       // epilogue may not have waited for the last MMAs, so wait for them here
       mma_commit(mma_done);
-      mbar_wait_drain(mma_done, 0);
+      mbar_wait_drain(mma_done, 0, ws->expired);
     }
   } else {
     // ----------------------------------------------------------- epilogue
@@ -807,7 +799,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const bool first = ch == 0, last = ch + 1 >= nch;
         const int a = (int)(g & 1u);
         if (nch > 0) {
-          if (!mbar_wait(&chunk_full[a], (g >> 1) & 1u, abort_flag)) {
+          if (!mbar_wait(&chunk_full[a], (g >> 1) & 1u, ws)) {
             ok = false;
             break;
           }

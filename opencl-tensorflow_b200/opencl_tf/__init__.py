@@ -23,7 +23,8 @@ Beyond the reference's op set: ``fused_ops`` (BatchNorm -> ReLU in one op),
 training step from one CUDA graph.
 """
 
-from ._library import raw_ops, fused_ops, step_ops, init, pool_stats, pool_trim, device_timeouts, library_path
+from ._library import (raw_ops, fused_ops, step_ops, init, pool_stats, pool_trim, device_timeouts, stream_status,
+                       set_wait_limit_ns, library_path)
 from .ops import (
     conv2d,
     conv2d_backprop_input,
@@ -60,7 +61,8 @@ __all__ = [
     "dense", "dense_backprop_input", "dense_backprop_weight", "dense_backprop_bias",
     "upsampling_bilinear_2d", "upsampling_bilinear_2d_grad",
     "fused_ops", "step_ops", "optimizers",
-    "layers", "errors", "init", "pool_stats", "pool_trim", "device_timeouts", "library_path",
+    "layers", "errors", "init", "pool_stats", "pool_trim", "device_timeouts", "stream_status",
+    "set_wait_limit_ns", "library_path",
 ]
 
 __version__ = "0.3.0+b200"

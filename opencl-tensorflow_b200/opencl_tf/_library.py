@@ -86,6 +86,8 @@ _SIGS = {
     "b2_adam_update": [_P, _I, _P, _P, _P, _P, _P, _F32, _F32, _F32, _F32, _F32, _F32, _P, _P],
     "b2_pool_trim": [],
     "b2_device_timeouts": [ctypes.POINTER(ctypes.c_uint)],
+    "b2_stream_status": [_P],
+    "b2_set_wait_limit_ns": [ctypes.c_uint64],
     "b2_kernel_launch_count": [ctypes.POINTER(ctypes.c_uint64)],
 }
 for _name, _args in _SIGS.items():
@@ -635,6 +637,27 @@ def _apply(op_type: str, kernel, inputs, attrs, nondiff=()):
 
 # --------------------------------------------------------------- raw_ops
 
+# B2_NVTX=1: every op call is an NVTX range named after the op (for nsys /
+# ncu --nvtx filtering), the tracing hook the reference's roadmap plans.
+_NVTX = os.environ.get("B2_NVTX", "0") not in ("", "0")
+
+
+def _traced(name: str, fn):
+    if not _NVTX:
+        return fn
+
+    def wrapper(*args, **kwargs):
+        torch.cuda.nvtx.range_push(name)
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    wrapper.__name__ = fn.__name__
+    wrapper.__doc__ = fn.__doc__
+    return wrapper
+
+
 def _mk_raw_ops():
     ns = types.SimpleNamespace()
 
@@ -702,7 +725,7 @@ def _mk_raw_ops():
 
     for k, v in list(locals().items()):
         if k.startswith("opencl_"):
-            setattr(ns, k, v)
+            setattr(ns, k, _traced(k, v))
     return ns
 
 
@@ -729,9 +752,8 @@ def _mk_fused_ops():
         """relu(x @ W + b) with the ReLU in the GEMM's epilogue."""
         return _apply("OpenclDenseRelu", _k_dense_relu, (x, w, b), {})
 
-    ns.opencl_batch_norm_relu_training = opencl_batch_norm_relu_training
-    ns.opencl_batch_norm_relu_grad = opencl_batch_norm_relu_grad
-    ns.opencl_dense_relu = opencl_dense_relu
+    for k in ("opencl_batch_norm_relu_training", "opencl_batch_norm_relu_grad", "opencl_dense_relu"):
+        setattr(ns, k, _traced(k, locals()[k]))
     return ns
 
 
@@ -751,8 +773,8 @@ def _mk_step_ops():
     def opencl_mse_loss_grad(y_pred, y_true, grad_loss):
         return _k_mse_loss_grad(y_pred, y_true, grad_loss)
 
-    ns.opencl_mse_loss = opencl_mse_loss
-    ns.opencl_mse_loss_grad = opencl_mse_loss_grad
+    ns.opencl_mse_loss = _traced("opencl_mse_loss", opencl_mse_loss)
+    ns.opencl_mse_loss_grad = _traced("opencl_mse_loss_grad", opencl_mse_loss_grad)
     return ns
 
 
@@ -789,6 +811,22 @@ def device_timeouts() -> int:
     c = ctypes.c_uint(0)
     _check(_lib.b2_device_timeouts(ctypes.byref(c)))
     return int(c.value)
+
+
+def stream_status(device=None) -> None:
+    """Synchronises torch's current stream of ``device`` and raises
+    :class:`opencl_tf.errors.DeadlineExceededError` if a bounded device-side
+    wait of one of this library's kernels expired since the last check (the
+    state is then cleared).  Until then every op call raises that error too."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _check(_lib.b2_stream_status(torch.cuda.current_stream(dev).cuda_stream))
+
+
+def set_wait_limit_ns(limit_ns: int) -> None:
+    """Limit of each bounded device-side wait for kernels launched from now on
+    (0 restores the 10 s default); a test hook."""
+    _check(_lib.b2_set_wait_limit_ns(int(limit_ns)))
 
 
 def upsampling_coords(in_size: int, out_size: int, device=None):

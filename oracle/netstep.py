@@ -20,6 +20,75 @@ def params_of(model):
     return p
 
 
+def _glorot_uniform(rng, shape):
+    """Keras's default kernel initializer: U(-l, l), l = sqrt(6 / (fan_in +
+    fan_out)), fans of a [..., in, out] kernel scaled by its receptive field."""
+    rf = int(np.prod(shape[:-2])) if len(shape) > 2 else 1
+    fi, fo = shape[-2] * rf, shape[-1] * rf
+    lim = np.sqrt(6.0 / max(1, fi + fo))
+    return rng.uniform(-lim, lim, shape).astype(np.float32)
+
+
+def readme_params(widened=False, seed=0):
+    """Random-init weights of the README network (README.md:162-183) without
+    the GPU package: glorot-uniform kernels, zero Dense bias, BatchNorm gamma 1
+    and beta 0, keyed like params_of().  ``widened``: input 256x256x3, filters
+    96/192/288, Dense 512."""
+    rng = np.random.default_rng(seed)
+    in_hw, filters, units = ((256, (96, 192, 288), 512) if widened else (64, (48, 96, 144), 128))
+    ones = lambda c: np.ones(c, np.float32)  # noqa: E731
+    zeros = lambda c: np.zeros(c, np.float32)  # noqa: E731
+    f0 = filters[0]
+    p = {"stem_w": _glorot_uniform(rng, (3, 7, 3, f0)), "stem_g": ones(f0), "stem_b": zeros(f0), "blocks": []}
+    H, W, C = in_hw, -(-in_hw // 2), f0
+    for f in filters[1:]:
+        p["blocks"].append({"dw": _glorot_uniform(rng, (3, 3, C, 1)), "g1": ones(C), "b1": zeros(C),
+                            "pw": _glorot_uniform(rng, (1, 1, C, f)), "g2": ones(f), "b2": zeros(f)})
+        H, W, C = -(-H // 2), -(-W // 2), f
+    p["dense_w"] = _glorot_uniform(rng, (H * W * C, units))
+    p["dense_b"] = zeros(units)
+    return p
+
+
+def uwb_seq(seed=0, t_ctx=8, n_bins=16, head=(9, 6, 8), eps=1e-3):
+    """Random-init stage list of the uwb_loc_v3 network
+    (examples/train_full_model.py:70-100) without the GPU package, in
+    seq_of()'s format: glorot-uniform kernels, zero Dense bias, BatchNorm
+    gamma 1, beta 0, moving mean 0, moving variance 1."""
+    rng = np.random.default_rng(seed)
+    st = []
+    H, W, C = t_ctx, n_bins, 36
+
+    def conv_bn_relu(f, k, s=(1, 1)):
+        nonlocal H, W, C
+        st.append(("conv", {"w": _glorot_uniform(rng, (k[0], k[1], C, f))}, ((1, s[0], s[1], 1), "SAME")))
+        H, W, C = -(-H // s[0]), -(-W // s[1]), f
+        st.append(("bn", {"g": np.ones(f, np.float32), "b": np.zeros(f, np.float32),
+                          "mean": np.zeros(f, np.float32), "var": np.ones(f, np.float32)}, eps))
+        st.append(("relu", {}, None))
+
+    conv_bn_relu(48, (3, 7), (1, 2))
+    for f in (96, 144, 192):
+        st.append(("dw", {"w": _glorot_uniform(rng, (3, 3, C, 1))}, ((1, 2, 2, 1), "SAME")))
+        H, W = -(-H // 2), -(-W // 2)
+        st.append(("bn", {"g": np.ones(C, np.float32), "b": np.zeros(C, np.float32),
+                          "mean": np.zeros(C, np.float32), "var": np.ones(C, np.float32)}, eps))
+        st.append(("relu", {}, None))
+        conv_bn_relu(f, (1, 1))
+    conv_bn_relu(64, (1, 1))
+    units = head[0] * head[1] * head[2]
+    st += [("flatten", {}, None),
+           ("dense", {"w": _glorot_uniform(rng, (H * W * C, units)), "b": np.zeros(units, np.float32)}, None),
+           ("relu", {}, None), ("reshape", {}, tuple(head))]
+    H, W, C = head
+    for _ in range(2):
+        st.append(("up", {}, (2, 2)))
+        H, W = 2 * H, 2 * W
+        conv_bn_relu(16, (3, 3))
+    st += [("conv", {"w": _glorot_uniform(rng, (1, 1, C, 1))}, ((1, 1, 1, 1), "SAME")), ("sigmoid", {}, None)]
+    return st
+
+
 def train_grads(o, p, x, target, head=(4, 4, 8), up=(2, 2), eps=1e-3):
     """Returns (loss, out, grads) with grads keyed like params_of()."""
     S1 = (1, 1, 2, 1)

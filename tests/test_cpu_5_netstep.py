@@ -194,3 +194,46 @@ def test_uwb_input_permute():
     y = uwb_input(x)
     assert y.shape == (2, 8, 16, 36)
     assert y[1, 5, 11, 4 * 6 + 2 * 2 + 1] == x[1, 5, 4, 2, 11, 1]
+
+
+@pytest.mark.parametrize("widened", [False, True])
+def test_numpy_readme_params_match_the_model(widened):
+    """The bench reference arm's numpy weights have the model's structure and
+    shapes, and the Keras initial values (glorot-uniform bounds, gamma 1, beta
+    0, zero bias)."""
+    from opencl_tf.model import build_model
+    from oracle.netstep import params_of, readme_params
+    want = params_of(build_model(widened=widened))
+    got = readme_params(widened=widened, seed=0)
+
+    def flat(p, pre=""):
+        out = {}
+        for k, v in p.items():
+            if isinstance(v, list):
+                for i, d in enumerate(v):
+                    out.update(flat(d, f"{pre}{k}{i}."))
+            else:
+                out[pre + k] = v
+        return out
+
+    fw, fg = flat(want), flat(got)
+    assert sorted(fw) == sorted(fg)
+    for k in fw:
+        assert fw[k].shape == fg[k].shape and fg[k].dtype == np.float32, k
+        if k.endswith(("_g", ".g1", ".g2")):
+            assert (fg[k] == 1).all(), k
+        elif k.endswith(("_b", ".b1", ".b2")):
+            assert (fg[k] == 0).all(), k
+        else:
+            assert np.abs(fg[k]).max() <= np.abs(fw[k]).max() * 1.05 + 1e-6, k
+
+
+def test_numpy_uwb_seq_matches_the_model(uwb):
+    from oracle.netstep import uwb_seq
+    got = uwb_seq(seed=0)
+    assert [k for k, _, _ in got] == [k for k, _, _ in uwb]
+    for (k, p, a), (_, q, b) in zip(got, uwb):
+        assert sorted(p) == sorted(q), k
+        for n in p:
+            assert p[n].shape == q[n].shape, (k, n)
+        assert a == b, (k, a, b)

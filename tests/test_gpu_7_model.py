@@ -38,9 +38,9 @@ def _grad_pairs(m, g):
     return out
 
 
-@pytest.mark.parametrize("batch", [2, 4, 8])
-def test_build_model_step_matches_oracle(otf, port, batch):
-    """Loss, output and all 17 weight gradients.  Each gradient must be within
+def _check_step(m, x, t, port, head=(4, 4, 8)):
+    """Loss, output and all 17 weight gradients of one training step of `m`
+    on (x, t) against the oracle-composed step.  Each gradient must be within
     the contract tolerance of the oracle (the reference's arithmetic); where
     the oracle itself is farther than that from the float64 answer (the
     stem and first depthwise filter gradients: BN backward amplifies the
@@ -48,14 +48,12 @@ def test_build_model_step_matches_oracle(otf, port, batch):
     within the tolerance of float64 and no farther from it than the oracle."""
     from opencl_tf.train import mse
     from oracle.netstep import train_grads_f64
-    m = _model()
-    x, t = _batch(batch)
     p = params_of(m)
     out = m(torch.from_numpy(x).cuda(), training=True)
     loss = mse(out, torch.from_numpy(t).cuda())
     loss.backward()
-    r_loss, r_out, r_g = train_grads(port, p, x, t)
-    e_loss, e_out, e_g = train_grads_f64(p, x, t, device="cuda")
+    r_loss, r_out, r_g = train_grads(port, p, x, t, head=head)
+    e_loss, e_out, e_g = train_grads_f64(p, x, t, head=head, device="cuda")
     assert abs(float(loss.detach()) - r_loss) <= 1e-5 * abs(r_loss)
     assert_close(to_np(out), r_out, what="output")
     report = []
@@ -70,6 +68,27 @@ def test_build_model_step_matches_oracle(otf, port, batch):
         assert vs_exact[1] <= ref_vs_exact[1], (name, vs_exact, ref_vs_exact)
     print("\n".join(f"{n:8s} gpu-vs-oracle {a[0]:.1e}/{a[1]:.1e}  oracle-vs-f64 {b[0]:.1e}/{b[1]:.1e}  "
                     f"gpu-vs-f64 {c[0]:.1e}/{c[1]:.1e}" for n, a, b, c in report))
+
+
+# 256 is the benchmarked batch (bench.py's README step): the BatchNorm
+# statistics then run over 524,288 rows per channel at the stem.
+@pytest.mark.parametrize("batch", [2, 4, 8, 256])
+def test_build_model_step_matches_oracle(otf, port, batch):
+    x, t = _batch(batch)
+    _check_step(_model(), x, t, port)
+
+
+def test_widened_build_model_step_matches_oracle(otf, port):
+    """The widened variant's layer shapes (input 256x256x3, filters 96/192/288,
+    Dense 589,824 x 512, head 8x8x8 -> 16x16x8) at batch 2: every op of its
+    training step, composed, against the oracle."""
+    from opencl_tf.model import build_model
+    torch.manual_seed(0)
+    m = build_model(widened=True, device="cuda")
+    rng = np.random.default_rng(11)
+    x = rng.uniform(0, 1, (2, 256, 256, 3)).astype(np.float32)
+    t = rng.uniform(0, 1, (2, 16, 16, 8)).astype(np.float32)
+    _check_step(m, x, t, port, head=(8, 8, 8))
 
 
 def test_graphed_step_equals_eager_step(otf):

@@ -225,3 +225,19 @@ def test_tma_engine_repeated_standalone_calls(otf, shape):
     torch.cuda.synchronize()
     assert bad == 0
     assert otf.device_timeouts() == before
+
+
+def test_widened_dense_wgrad_full_k_against_float64(otf):
+    """The widened variant's Dense weight gradient at its full size: x
+    [128, 589824] (the flattened 64x32x288 activations of 128 images), dy
+    [128, 512] -> dW [589824, 512] (302 M entries, 1.2 GB) -- the step's
+    largest gradient and its largest all-reduce -- against float64."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.rand(128, 589824, device="cuda", generator=g)  # post-ReLU activations are >= 0
+    dy = torch.randn(128, 512, device="cuda", generator=g) * 1e-3
+    dw = otf.dense_backprop_weight(x, dy)
+    exact = x.double().t() @ dy.double()
+    d = (dw.double() - exact)
+    mx = float(d.abs().max() / exact.abs().max())
+    l2 = float(torch.linalg.vector_norm(d) / torch.linalg.vector_norm(exact))
+    assert mx <= 1e-4 and l2 <= 1e-5, (mx, l2)

@@ -62,7 +62,11 @@ def _allocs(lib):
     return s.num_allocs
 
 
-@pytest.mark.parametrize("shape", [(256, 64, 32, 48), (7, 5, 9, 6)])
+# (256, 64, 32, 48) and (7, 5, 9, 6) keep the pooled entry point's row blocks;
+# the others have so many channels that the row blocks are capped to fit the
+# fixed array (C = 256: at most 127 blocks, 4096: 7, 16384: 1).
+@pytest.mark.parametrize("shape", [(256, 64, 32, 48), (7, 5, 9, 6), (64, 32, 32, 256), (2, 8, 8, 4096),
+                                   (1, 4, 4, 16384)])
 def test_no_alloc_matches_pooled_entry_point_two_calls(lib, shape):
     torch.manual_seed(1)
     C = shape[3]
@@ -79,6 +83,12 @@ def test_no_alloc_matches_pooled_entry_point_two_calls(lib, shape):
         want = _run(lib, "b2_batch_norm_training", x, g, b)
         for name, a, w in zip(("y", "mean", "var"), outs, want):
             assert_close(a.cpu().numpy(), w.cpu().numpy(), what=name)
+        # and the statistics against float64: biased variance E[x^2] - mean^2
+        xd = x.double().reshape(-1, C).cpu().numpy()
+        m64 = xd.mean(axis=0)
+        v64 = (xd * xd).mean(axis=0) - m64 * m64
+        assert_close(outs[1].cpu().numpy(), m64, what="mean vs float64")
+        assert_close(outs[2].cpu().numpy(), v64, what="var vs float64")
 
 
 def test_no_alloc_rejects_too_many_channels(lib):
