@@ -437,7 +437,17 @@ def main():
     ap.add_argument("--widened", action="store_true")
     ap.add_argument("--model", choices=["build_model", "uwb_loc_v3"], default="build_model")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--stress-gemm", action="store_true",
+                    help="time the 8192x4096x4096 stress GEMM's three passes (one JSON line) and exit")
     args = ap.parse_args()
+    if args.stress_gemm:
+        import torch
+        import opencl_tf  # noqa: F401
+        from opencl_tf import profile
+        torch.cuda.set_device(0)
+        print(json.dumps({"workload": "stress GEMM M=8192 K=4096 N=4096 fp32 ~N(0,1) (Dense fwd / dgrad / wgrad)",
+                          **profile.stress_gemm(torch.device("cuda", 0), reps=max(args.steps, 3))}), flush=True)
+        return 0
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))

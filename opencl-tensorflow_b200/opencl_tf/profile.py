@@ -170,6 +170,39 @@ def summarize(rows) -> dict:
 
 
 
+def stress_gemm_inputs(device, m=8192, k=4096, n=4096, seed=0):
+    """The tensor-core stress case of the Dense + head workload: x [m, k], W
+    [k, n], dy [m, n], all ~N(0, 1), b = 0."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(m, k, device=device, generator=g)
+    w = torch.randn(k, n, device=device, generator=g)
+    dy = torch.randn(m, n, device=device, generator=g)
+    return x, w, torch.zeros(n, device=device), dy
+
+
+def stress_gemm(device=None, reps=10) -> dict:
+    """Times the stress GEMM's three passes (Dense forward M=8192, N=4096,
+    K=4096; input gradient; weight gradient, K=8192), each 2*8192*4096*4096 =
+    274.9 GFLOP: ms per pass (L2 flushed between repetitions), TFLOP/s and the
+    fraction of the 3xTF32 ceiling (the bf16 tensor peak / 6)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    x, w, b, dy = stress_gemm_inputs(dev)
+    flush = _Flusher(dev)
+    pk = peaks()
+    ceiling = tf32x3_peak_tflops(pk)
+    flops = 2.0 * x.shape[0] * x.shape[1] * w.shape[1]
+    passes = {"forward": lambda: L._k_dense(x, w, b), "backprop_input": lambda: L._k_dense_backprop_input(dy, w),
+              "backprop_weight": lambda: L._k_dense_backprop_weight(x, dy)}
+    out = {}
+    for name, fn in passes.items():
+        ms = time_call(fn, reps=reps, flush=flush)
+        tf = flops / (ms * 1e-3) / 1e12
+        out[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac_3xtf32": round(tf / ceiling, 4)}
+    out["ceiling_tflops"] = round(ceiling, 1)
+    out["peak_source"] = pk["source"]
+    out["gflop_per_pass"] = round(flops / 1e9, 1)
+    return out
+
 
 def _cli() -> int:
     """Replay one op of a network's training step, e.g. for ncu:
@@ -191,7 +224,18 @@ def _cli() -> int:
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--list", action="store_true")
     ap.add_argument("--model", choices=["build_model", "uwb_loc_v3"], default="build_model")
+    ap.add_argument("--stress", choices=["forward", "backprop_input", "backprop_weight"],
+                    help="run one pass of the 8192x4096x4096 stress GEMM instead")
     a = ap.parse_args()
+    if a.stress:
+        dev = torch.device("cuda", 0)
+        x, w, b, dy = stress_gemm_inputs(dev)
+        fn = {"forward": lambda: L._k_dense(x, w, b), "backprop_input": lambda: L._k_dense_backprop_input(dy, w),
+              "backprop_weight": lambda: L._k_dense_backprop_weight(x, dy)}[a.stress]
+        for _ in range(1 + a.reps):
+            fn()
+        torch.cuda.synchronize()
+        return 0
     from .model import build_model, build_uwb_loc_v3
     from .train import mse
     dev = torch.device("cuda", 0)

