@@ -755,6 +755,7 @@ int b2_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int6
   const int64_t M = g.kH * g.kW * g.Ci, K = g.N * g.Ho * g.Wo;
   if (M == 0 || g.Co == 0) return B2_OK;
   if (conv_direct_ok(g)) return conv_direct_backprop_filter(g, input, out_backprop, output, s);
+  if (conv_wgrad_rows_ok(g, out_backprop, nullptr)) return conv_wgrad_rows(g, input, out_backprop, output, s);
   const MNMajor bv{out_backprop, g.Co, g.Co};
   if (is_pointwise(g)) {
     const MNMajor av{input, g.Ci, g.Ci};
