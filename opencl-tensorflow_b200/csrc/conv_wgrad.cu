@@ -383,8 +383,9 @@ extern "C" int b2_conv2d_batch_norm_relu_backprop_filter(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows = g.N * g.Ho * g.Wo;
   if (g.Co == 0) return B2_OK;
-  if (!conv_wgrad_rows_ok(g, grad_z, bn_input) || rows == 0) {
-    // any other shape: the two ops in sequence, the input gradient in scratch
+  if (conv_direct_ok(g) || !conv_wgrad_rows_ok(g, grad_z, bn_input) || rows == 0) {
+    // any shape b2_conv2d_backprop_filter does not give to this kernel: the
+    // two ops in sequence, the input gradient in scratch
     Scratch dx;
     B2_RETURN_IF_ERROR(dx.alloc(sizeof(float) * (size_t)(rows * g.Co > 0 ? rows * g.Co : 1), s));
     B2_RETURN_IF_ERROR(b2_batch_norm_relu_grad(stream, grad_z, out_shape, bn_input, out_shape, gamma, beta,
