@@ -20,10 +20,10 @@
 // against one 16-byte load of dy and 1.5 of x.
 //
 // Work unit: one output row (n, ho), or a chunk of Wc of its columns.  A CTA
-// (one per SM) walks a contiguous range of units; all its threads stage a
-// unit -- the dy chunk and the kH input row segments it reads, zero-filled
-// outside the image -- with cp.async into one of two buffers while computing
-// on the other.  Teams of kH * Co/4 threads split the unit's columns.  At the
+// (one per SM) walks a contiguous range of units; all its threads stage
+// units -- the dy chunk and the kH input row segments it reads, zero-filled
+// outside the image -- with cp.async into a ring of buffers, several units
+// ahead of the one they compute on.  Teams of kH * Co/4 threads split the unit's columns.  At the
 // end the CTA folds its teams in team order and writes one partial per filter
 // element; a second kernel adds the CTA partials in block order, so results
 // are deterministic.
@@ -43,6 +43,7 @@ namespace {
 
 constexpr int kWgThreads = 288;  // 9 warps
 constexpr int kWgWpt = 4;        // output columns per thread per unit
+constexpr int kWgStages = 6;     // unit buffers: 5 units in flight while one is computed
 constexpr int kWgConsts = 7;     // fused: mean, inv_std, k1, grad_beta, grad_gamma, gamma, beta
 
 struct WgGeom {
@@ -87,9 +88,11 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Shared-memory plan (floats): [fused constants 7 x Co] then two unit buffers
-// (dy chunk [Wc][Co], fused: BN-input chunk [Wc][Co], input rows [kH][seg]),
-// overlaid after the walk by the team fold [teams][team][KWC][4].
+// Shared-memory plan (floats): [fused constants 7 x Co] then kWgStages unit
+// buffers (dy chunk [Wc][Co], fused: BN-input chunk [Wc][Co], input rows
+// [kH][seg]), overlaid after the walk by the team fold [teams][team][KWC][4].
+// One CTA per SM computes a unit in ~0.4 us; a DRAM round trip takes longer,
+// so several units must be in flight at once.
 struct WgSmem {
   int consts, buf, fold, total;
 };
@@ -100,7 +103,7 @@ __host__ __device__ inline WgSmem wg_smem(const WgGeom& g, bool fused) {
   s.consts = fused ? kWgConsts * g.Co : 0;
   s.buf = g.Wc * g.Co * (fused ? 2 : 1) + g.kH * g.seg;
   s.fold = g.teams * g.team * KWC * 4;
-  const int body = 2 * s.buf > s.fold ? 2 * s.buf : s.fold;
+  const int body = kWgStages * s.buf > s.fold ? kWgStages * s.buf : s.fold;
   s.total = s.consts + body;
   return s;
 }
@@ -169,14 +172,23 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 
   const int u_begin = blockIdx.x * g.upb;
   const int u_end = u_begin + g.upb < g.units ? u_begin + g.upb : g.units;
-  if (u_begin < u_end) stage(u_begin, 0);
-  cp_async_commit();
-  for (int u = u_begin; u < u_end; ++u) {
-    const int b = (u - u_begin) & 1;
-    if (u + 1 < u_end) stage(u + 1, b ^ 1);
+  // ring: unit u_begin + i lives in buffer i % kWgStages; one commit group per
+  // unit (empty past the end), so "at most kWgStages - 1 groups pending" means
+  // the oldest unit has landed
+#pragma unroll 1
+  for (int j = 0; j < kWgStages - 1; ++j) {
+    if (u_begin + j < u_end) stage(u_begin + j, j);
     cp_async_commit();
-    cp_async_wait<1>();  // this thread's copies of unit u have landed
-    __syncthreads();     // ... and everyone's
+  }
+  for (int u = u_begin; u < u_end; ++u) {
+    const int i = u - u_begin;
+    const int b = i % kWgStages;
+    // the buffer unit u + kWgStages - 1 takes was computed on last iteration,
+    // before its closing barrier
+    if (u + kWgStages - 1 < u_end) stage(u + kWgStages - 1, (i + kWgStages - 1) % kWgStages);
+    cp_async_commit();
+    cp_async_wait<kWgStages - 1>();  // this thread's copies of unit u have landed
+    __syncthreads();                 // ... and everyone's
     float* buf = body + b * plan.buf;
     if (FUSED) {
       // dy = BatchNorm -> ReLU backward of (dz, y), in place of dz
@@ -222,7 +234,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) acc[k][c] = fmaf(win[i * STEP + k], d[i][c], acc[k][c]);
     }
-    __syncthreads();  // buffer b is restaged two units from now
+    __syncthreads();  // buffer b is restaged by the next iteration
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -291,6 +303,12 @@ bool conv_wgrad_rows_ok(const ConvGeom& g, const float* dy, const float* ybn) {
   if (!aligned16(dy) || (ybn != nullptr && !aligned16(ybn))) return false;
   const int64_t teams = kWgThreads / (g.kH * g.Co / 4);
   const int64_t wc = teams * kWgWpt;
+  // shared memory (the fused plan is the larger): 7 constants per channel, the
+  // ring of unit buffers or the team fold, within the 227 KB a CTA may use
+  const int64_t seg = ((wc - 1) * kStemSW + kStemKW) * kStemCI + 8;
+  const int64_t ring = kWgStages * (wc * g.Co * 2 + g.kH * seg);
+  const int64_t fold = kWgThreads * kStemKW * kStemCI * 4;
+  if (4 * (kWgConsts * g.Co + (ring > fold ? ring : fold)) > 227 * 1024) return false;
   return g.N * g.Ho * ceil_div(g.Wo, wc) <= INT_MAX && g.H <= INT_MAX && g.W <= INT_MAX;
 }
 

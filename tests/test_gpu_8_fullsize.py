@@ -167,6 +167,7 @@ def test_long_reductions_against_float64(otf):
     """The README stem's filter gradient at batch 256 (K = 524288 pixels) and a
     K = 65536 dense product: fp32-class accuracy against float64."""
     torch.manual_seed(4)
+    before = otf.device_timeouts()  # cumulative over the process
     x = torch.rand(256, 64, 64, 3, device="cuda")
     dy = torch.randn(256, 64, 32, 48, device="cuda")
     dw = otf.conv2d_backprop_filter(x, [3, 7, 3, 48], dy, strides=(1, 1, 2, 1), padding="SAME")
@@ -178,7 +179,7 @@ def test_long_reductions_against_float64(otf):
     y = otf.dense(a, w, torch.zeros(256, device="cuda"))
     mx, l2 = rel_errs(to_np(y), (a.double() @ w.double()).cpu().numpy())
     assert mx <= 1e-4 and l2 <= 1e-5, ("dense K=65536", mx, l2)
-    assert otf.device_timeouts() == 0
+    assert otf.device_timeouts() == before
 
 
 def test_full_size_ops_are_deterministic(otf):
