@@ -20,15 +20,28 @@
 // against one 16-byte load of dy and 1.5 of x.
 //
 // Work unit: one output row (n, ho), or a chunk of Wc of its columns.  A CTA
-// (one per SM) walks a contiguous range of units; all its threads stage
-// units -- the dy chunk and the kH input row segments it reads, zero-filled
-// outside the image -- with cp.async into a ring of buffers, several units
-// ahead of the one they compute on.  Teams of kH * Co/4 threads split the unit's columns.  At the
-// end the CTA folds its teams in team order and writes one partial per filter
-// element; a second kernel adds the CTA partials in block order, so results
-// are deterministic.
+// (one per SM) walks a contiguous range of units through a ring of
+// shared-memory slots, with three warp roles and no block-wide barrier:
 //
-// FUSED: dy is not read but computed while staged, from the BatchNorm ->
+//   warp 0        lane 0 stages a unit with 1-D bulk copies (cp.async.bulk,
+//                 completion on the slot's FULL mbarrier): the dy chunk (a
+//                 contiguous span of the NHWC tensor) and the kH whole input
+//                 rows it reads, each placed between zero margins that the
+//                 copies never touch, so every tap of every column lands
+//                 inside the slot; input rows outside the image are flagged;
+//   warps 1..2    (FUSED) compute dy = the BatchNorm -> ReLU backward of the
+//                 staged dz and y, with the per-channel constants in
+//                 registers, into the slot, and arrive on DX_READY;
+//   warps 3..     consumers: teams of kH * Co/4 threads split the unit's
+//                 columns; each thread loads its input window (kW*Ci + 3*sW*Ci
+//                 floats) and its 4 x 4 dy values and issues the FMAs, then
+//                 its warp arrives on EMPTY.
+//
+// Every wait is bounded.  At the end the CTA folds its teams in team order
+// and writes one partial per filter element; a second kernel adds the CTA
+// partials in block order, so results are deterministic.
+//
+// FUSED: dy is not read but computed in shared memory from the BatchNorm ->
 // ReLU backward's inputs (dz and the BN input y) and its per-channel
 // constants, with the same arithmetic as the BatchNorm dx pass (so the filter
 // gradient equals the unfused sequence's bit for bit), and never written to
@@ -39,23 +52,33 @@
 #include "conv_common.cuh"
 
 namespace b2 {
+
+static __device__ unsigned int g_wg_timeouts = 0;
+
 namespace {
 
-constexpr int kWgThreads = 288;  // 9 warps
-constexpr int kWgWpt = 4;        // output columns per thread per unit
-constexpr int kWgStages = 6;     // unit buffers: 5 units in flight while one is computed
-constexpr int kWgConsts = 7;     // fused: mean, inv_std, k1, grad_beta, grad_gamma, gamma, beta
+constexpr int kWgConsumers = 288;  // 9 consumer warps
+constexpr int kWgDxWarps = 2;      // FUSED: dx warps
+constexpr int kWgWpt = 4;          // output columns per consumer thread per unit
+constexpr int kWgMaxStages = 6;
+constexpr int kWgPadL = 4;         // zero pixels staged before each input row
+
+__host__ __device__ constexpr int wg_threads(bool fused) {
+  return 32 * (1 + (fused ? kWgDxWarps : 0) + kWgConsumers / 32);
+}
 
 struct WgGeom {
   int N, H, W, Co, kH, sH, pH, pW, Ho, Wo;
-  int teams;      // teams per CTA
-  int team;       // threads per team: kH * Co / 4
-  int Wc;         // output columns per unit: teams * kWgWpt
-  int chunks;     // units per output row
-  int seg;        // staged floats per input row (multiple of 4)
-  int seg_valid;  // of which real input positions: ((Wc - 1) * sW + kW) * Ci
-  int units;      // N * Ho * chunks
-  int upb;        // units per CTA
+  int teams;   // consumer teams
+  int team;    // threads per team: kH * Co / 4
+  int Wc;      // output columns per unit: teams * kWgWpt
+  int chunks;  // units per output row
+  int xp;      // staged floats per input row: zero margin, W*Ci values, zero margin (multiple of 4)
+  int slot;    // floats per slot
+  int stages;  // slots
+  int units;   // N * Ho * chunks
+  int upb;     // units per CTA
+  WaitParams wait;
 };
 
 struct BnDx {
@@ -67,180 +90,261 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// 16- / 4-byte asynchronous copies into shared memory; `valid` false writes
-// zeros and reads nothing (src-size 0; src is then any valid address).
-__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
-               "r"(valid ? 16u : 0u)
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(b)) : "memory");
+}
+
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes)
                : "memory");
 }
 
-__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src),
-               "r"(valid ? 4u : 0u)
+__device__ __forceinline__ bool bar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase of parity `parity`, at most limit_ns (or until another
+// wait of the CTA gave up: *abort); an expiry is counted, raises *abort and
+// sets the library's host-mapped expiry word.
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, const WaitParams& wp, volatile int* abort) {
+  if (bar_try_wait(b, parity)) return true;
+  const uint64_t t0 = now_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (bar_try_wait(b, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (now_ns() - t0 > wp.limit_ns) {
+        atomicAdd(&g_wg_timeouts, 1u);
+        *abort = 1;
+        if (wp.expired) {
+          *reinterpret_cast<volatile unsigned int*>(wp.expired) = 1u;
+          __threadfence_system();
+        }
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(float* dst, const float* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
                : "memory");
 }
 
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Slot layout (floats): dy (or dz) chunk [Wc][Co]; FUSED: BN-input chunk
+// [Wc][Co] and the computed dy chunk [Wc][Co]; then kH input rows [xp].
+__host__ __device__ inline int wg_slot_floats(int Wc, int Co, int kH, int xp, bool fused) {
+  return Wc * Co * (fused ? 3 : 1) + kH * xp;
 }
 
-// Shared-memory plan (floats): [fused constants 7 x Co] then kWgStages unit
-// buffers (dy chunk [Wc][Co], fused: BN-input chunk [Wc][Co], input rows
-// [kH][seg]), overlaid after the walk by the team fold [teams][team][KWC][4].
-// One CTA per SM computes a unit in ~0.4 us; a DRAM round trip takes longer,
-// so several units must be in flight at once.
-struct WgSmem {
-  int consts, buf, fold, total;
-};
-
+// Dynamic shared memory: max(ring, team fold) + barriers and row flags.
 template <int KWC>
-__host__ __device__ inline WgSmem wg_smem(const WgGeom& g, bool fused) {
-  WgSmem s;
-  s.consts = fused ? kWgConsts * g.Co : 0;
-  s.buf = g.Wc * g.Co * (fused ? 2 : 1) + g.kH * g.seg;
-  s.fold = g.teams * g.team * KWC * 4;
-  const int body = kWgStages * s.buf > s.fold ? kWgStages * s.buf : s.fold;
-  s.total = s.consts + body;
-  return s;
+__host__ __device__ inline int wg_smem_bytes(const WgGeom& g) {
+  const int ring = g.stages * g.slot;
+  const int fold = g.teams * g.team * KWC * 4;
+  const int body = (ring > fold ? ring : fold) * 4;
+  return body + 8 * 3 * kWgMaxStages + 4 * kWgMaxStages * 8 + 16;
 }
 
 template <int KW, int CI, int SW, bool FUSED>
-__global__ void __launch_bounds__(kWgThreads, 1)
+__global__ void __launch_bounds__(wg_threads(FUSED), 1)
     conv_wgrad_rows_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                            const float* __restrict__ ybn, BnDx bn, WgGeom g, float* __restrict__ partial) {
   constexpr int KWC = KW * CI;
-  constexpr int STEP = SW * CI;                        // window shift per output column
-  constexpr int NWIN = (kWgWpt - 1) * STEP + KWC;      // floats of x a thread's columns read per kh
-  constexpr int NWIN4 = (NWIN + 3) / 4 * 4;
-  static_assert((kWgWpt * STEP) % 4 == 0, "team windows must start 16-byte aligned");
+  constexpr int STEP = SW * CI;                    // window shift per output column
+  constexpr int NWIN = (kWgWpt - 1) * STEP + KWC;  // floats of x a thread's columns read per filter row
+  constexpr int NWIN2 = (NWIN + 1) / 2 * 2;
+  constexpr int kConsumer0 = 32 * (1 + (FUSED ? kWgDxWarps : 0));
   extern __shared__ __align__(16) float wsm[];
-  const WgSmem plan = wg_smem<KWC>(g, FUSED);
-  const int tid = threadIdx.x;
-  const int Co = g.Co, cq = Co / 4;
+  const int S = g.stages, Co = g.Co, cq = Co / 4, chunk = g.Wc * Co;
+  const int fold_floats = g.teams * g.team * KWC * 4;
+  const int body = S * g.slot > fold_floats ? S * g.slot : fold_floats;
+  uint64_t* full = reinterpret_cast<uint64_t*>(wsm + body);
+  uint64_t* dxr = full + kWgMaxStages;
+  uint64_t* empty = dxr + kWgMaxStages;
+  int* rowok = reinterpret_cast<int*>(empty + kWgMaxStages);  // [S][kH]
+  __shared__ int s_abort;
+  volatile int* abort = &s_abort;
 
-  if (FUSED) {
-    for (int c = tid; c < Co; c += blockDim.x) {
-      wsm[c] = bn.mean[c];
-      wsm[Co + c] = bn.inv_std[c];
-      wsm[2 * Co + c] = bn.k1[c];
-      wsm[3 * Co + c] = bn.grad_beta[c];
-      wsm[4 * Co + c] = bn.grad_gamma[c];
-      wsm[5 * Co + c] = bn.gamma[c];
-      wsm[6 * Co + c] = bn.beta[c];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int u_begin = blockIdx.x * g.upb;
+  const int nu = (u_begin + g.upb < g.units ? u_begin + g.upb : g.units) - u_begin;
+  const int consumer_warps = (g.teams * g.team + 31) / 32;
+
+  // zero the ring once: the input rows' margins are never written again
+  for (int i = tid; i < S * g.slot; i += blockDim.x) wsm[i] = 0.0f;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (tid == 0) {
+    s_abort = 0;
+    for (int i = 0; i < S; ++i) {
+      bar_init(&full[i], 1);
+      bar_init(&dxr[i], kWgDxWarps);
+      bar_init(&empty[i], consumer_warps);
     }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  float* body = wsm + plan.consts;
+  __syncthreads();
 
-  // this thread's role: team (a group of Wc / teams output columns), filter
-  // row kh, output channels 4*cg .. 4*cg+3
-  const int team = tid / g.team, r = tid - team * g.team;
-  const int kh = r / cq, cg = r - kh * cq;
-  const bool computes = team < g.teams;
-
-  auto stage = [&](int u, int b) {
-    const int row = u / g.chunks, c = u - row * g.chunks;  // row = n * Ho + ho
-    const int n = row / g.Ho, ho = row - n * g.Ho;
-    const int wo0 = c * g.Wc;
-    float* buf = body + b * plan.buf;
-    const int64_t d0 = ((int64_t)row * g.Wo + wo0) * Co;
-    const int nq = g.Wc * cq;
-    for (int i = tid; i < nq; i += blockDim.x) {
-      const bool ok = wo0 + i / cq < g.Wo;
-      const int64_t off = d0 + 4 * (int64_t)i;
-      cp_async16(buf + 4 * i, ok ? dy + off : dy, ok);
-      if (FUSED) cp_async16(buf + g.Wc * Co + 4 * i, ok ? ybn + off : ybn, ok);
-    }
-    float* xs = buf + g.Wc * Co * (FUSED ? 2 : 1);
-    const int w0 = SW * wo0 - g.pW;  // input column of staged position 0
-    const int nx = g.kH * g.seg;
-    for (int i = tid; i < nx; i += blockDim.x) {
-      const int rk = i / g.seg, j = i - rk * g.seg;
-      const int hi = ho * g.sH - g.pH + rk;
-      const int wi = w0 + j / CI, ci = j - (j / CI) * CI;
-      const bool ok = j < g.seg_valid && hi >= 0 && hi < g.H && wi >= 0 && wi < g.W;
-      cp_async4(xs + i, ok ? x + (((int64_t)n * g.H + hi) * g.W + wi) * CI + ci : x, ok);
-    }
-  };
-
+  const int xrow0 = chunk * (FUSED ? 3 : 1);  // offset of the input rows in a slot
   float acc[KWC][4];
 #pragma unroll
   for (int k = 0; k < KWC; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
+  const int ct = tid - kConsumer0;
+  const int team = ct >= 0 ? ct / g.team : g.teams, r = ct >= 0 ? ct - team * g.team : 0;
+  const int kh = r / cq, cg = r - kh * cq;
 
-  const int u_begin = blockIdx.x * g.upb;
-  const int u_end = u_begin + g.upb < g.units ? u_begin + g.upb : g.units;
-  // ring: unit u_begin + i lives in buffer i % kWgStages; one commit group per
-  // unit (empty past the end), so "at most kWgStages - 1 groups pending" means
-  // the oldest unit has landed
-#pragma unroll 1
-  for (int j = 0; j < kWgStages - 1; ++j) {
-    if (u_begin + j < u_end) stage(u_begin + j, j);
-    cp_async_commit();
-  }
-  for (int u = u_begin; u < u_end; ++u) {
-    const int i = u - u_begin;
-    const int b = i % kWgStages;
-    // the buffer unit u + kWgStages - 1 takes was computed on last iteration,
-    // before its closing barrier
-    if (u + kWgStages - 1 < u_end) stage(u + kWgStages - 1, (i + kWgStages - 1) % kWgStages);
-    cp_async_commit();
-    cp_async_wait<kWgStages - 1>();  // this thread's copies of unit u have landed
-    __syncthreads();                 // ... and everyone's
-    float* buf = body + b * plan.buf;
-    if (FUSED) {
-      // dy = BatchNorm -> ReLU backward of (dz, y), in place of dz
-      const int row = u / g.chunks;
-      const int wo0 = (u - row * g.chunks) * g.Wc;
-      const float* yb = buf + g.Wc * Co;
-      const float* cs = wsm;
-      for (int e = tid; e < g.Wc * Co; e += blockDim.x) {
-        const int wl = e / Co, ch = e - wl * Co;
-        float v = 0.0f;
-        if (wo0 + wl < g.Wo)
-          v = bn_grad_dx_value<true>(yb[e], buf[e], cs[ch], cs[Co + ch], cs[2 * Co + ch], cs[3 * Co + ch],
-                                     cs[4 * Co + ch], cs[5 * Co + ch], cs[6 * Co + ch], bn.nhw_f);
-        buf[e] = v;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nu; ++i, ++issued) {
+        const int sl = i % S;
+        if (i >= S && !bar_wait(&empty[sl], (uint32_t)(i / S - 1) & 1u, g.wait, abort)) break;
+        const int u = u_begin + i;
+        const int row = u / g.chunks, c = u - row * g.chunks;
+        const int n = row / g.Ho, ho = row - n * g.Ho;
+        const int wo0 = c * g.Wc;
+        const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
+        float* base = wsm + (size_t)sl * g.slot;
+        uint32_t bytes = (uint32_t)(nv * Co * 4) * (FUSED ? 2u : 1u);
+        for (int k = 0; k < g.kH; ++k) {
+          const int hi = ho * g.sH - g.pH + k;
+          const bool ok = hi >= 0 && hi < g.H;
+          rowok[sl * g.kH + k] = ok;
+          if (ok) bytes += (uint32_t)(g.W * CI * 4);
+        }
+        bar_expect_tx(&full[sl], bytes);
+        const int64_t d0 = ((int64_t)row * g.Wo + wo0) * Co;
+        bulk_g2s(base, dy + d0, (uint32_t)(nv * Co * 4), &full[sl]);
+        if (FUSED) bulk_g2s(base + chunk, ybn + d0, (uint32_t)(nv * Co * 4), &full[sl]);
+        for (int k = 0; k < g.kH; ++k) {
+          const int hi = ho * g.sH - g.pH + k;
+          if (hi >= 0 && hi < g.H)
+            bulk_g2s(base + xrow0 + k * g.xp + kWgPadL * CI, x + ((int64_t)n * g.H + hi) * g.W * CI,
+                     (uint32_t)(g.W * CI * 4), &full[sl]);
+        }
       }
-      __syncthreads();
+      // let every issued copy land before the CTA can leave its ring
+      const int first = issued > S ? issued - S : 0;
+      WaitParams drain = g.wait;
+      drain.limit_ns = kDefaultWaitLimitNs;
+      int no_abort = 0;
+      for (int i = first; i < issued; ++i)
+        bar_wait(&full[i % S], (uint32_t)(i / S) & 1u, drain, &no_abort);
     }
-    if (computes) {
-      const float* xs = buf + g.Wc * Co * (FUSED ? 2 : 1);
-      const float* xw = xs + kh * g.seg + team * kWgWpt * STEP;
-      float win[NWIN4];
+  } else if (FUSED && warp <= kWgDxWarps) {
+    // ------------------------------------------------------- dx (FUSED)
+    // thread t: channel group t % cq of rows t / cq, t / cq + lanes_per, ...
+    const int t = tid - 32, per = (32 * kWgDxWarps) / cq;
+    const bool active = t < per * cq;
+    const int dcg = active ? t % cq : 0, wl0 = t / cq;
+    float m[4], iv[4], k1[4], gb[4], gg[4], ga[4], be[4];
 #pragma unroll
-      for (int q = 0; q < NWIN4 / 4; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(xw + 4 * q);
-        win[4 * q] = v.x;
-        win[4 * q + 1] = v.y;
-        win[4 * q + 2] = v.z;
-        win[4 * q + 3] = v.w;
-      }
-      float d[kWgWpt][4];
-#pragma unroll
-      for (int i = 0; i < kWgWpt; ++i) {
-        const float4 v = *reinterpret_cast<const float4*>(buf + (team * kWgWpt + i) * Co + 4 * cg);
-        d[i][0] = v.x;
-        d[i][1] = v.y;
-        d[i][2] = v.z;
-        d[i][3] = v.w;
-      }
-#pragma unroll
-      for (int i = 0; i < kWgWpt; ++i)
-#pragma unroll
-        for (int k = 0; k < KWC; ++k)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) acc[k][c] = fmaf(win[i * STEP + k], d[i][c], acc[k][c]);
+    for (int j = 0; j < 4; ++j) {
+      const int ch = 4 * dcg + j;
+      m[j] = bn.mean[ch];
+      iv[j] = bn.inv_std[ch];
+      k1[j] = bn.k1[ch];
+      gb[j] = bn.grad_beta[ch];
+      gg[j] = bn.grad_gamma[ch];
+      ga[j] = bn.gamma[ch];
+      be[j] = bn.beta[ch];
     }
-    __syncthreads();  // buffer b is restaged by the next iteration
+    for (int i = 0; i < nu; ++i) {
+      const int sl = i % S;
+      if (!bar_wait(&full[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
+      const int u = u_begin + i;
+      const int wo0 = (u - (u / g.chunks) * g.chunks) * g.Wc;
+      const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
+      float* base = wsm + (size_t)sl * g.slot;
+      if (active) {
+        for (int wl = wl0; wl < nv; wl += per) {
+          const int e = wl * Co + 4 * dcg;
+          const float4 z4 = *reinterpret_cast<const float4*>(base + e);
+          const float4 y4 = *reinterpret_cast<const float4*>(base + chunk + e);
+          float4 o;
+          o.x = bn_grad_dx_value<true>(y4.x, z4.x, m[0], iv[0], k1[0], gb[0], gg[0], ga[0], be[0], bn.nhw_f);
+          o.y = bn_grad_dx_value<true>(y4.y, z4.y, m[1], iv[1], k1[1], gb[1], gg[1], ga[1], be[1], bn.nhw_f);
+          o.z = bn_grad_dx_value<true>(y4.z, z4.z, m[2], iv[2], k1[2], gb[2], gg[2], ga[2], be[2], bn.nhw_f);
+          o.w = bn_grad_dx_value<true>(y4.w, z4.w, m[3], iv[3], k1[3], gb[3], gg[3], ga[3], be[3], bn.nhw_f);
+          *reinterpret_cast<float4*>(base + 2 * chunk + e) = o;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(&dxr[sl]);
+    }
+  } else if (ct >= 0 && ct < consumer_warps * 32) {
+    // ----------------------------------------------------------- consumers
+    const bool active = team < g.teams;
+    for (int i = 0; i < nu; ++i) {
+      const int sl = i % S;
+      // FULL (the staged input rows: completed before DX_READY, so this returns
+      // at once in the fused kernel, but it makes the bulk copies' writes
+      // visible to this thread directly) then, fused, DX_READY
+      if (!bar_wait(&full[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
+      if (FUSED && !bar_wait(&dxr[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
+      const int u = u_begin + i;
+      const int wo0 = (u - (u / g.chunks) * g.chunks) * g.Wc;
+      const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
+      const int col0 = team * kWgWpt;  // first column of this team in the unit
+      const float* base = wsm + (size_t)sl * g.slot;
+      if (active && col0 < nv && rowok[sl * g.kH + kh]) {
+        // window: staged position (padL + sW * (wo0 + col0) - pW) * Ci of row kh
+        const float* xw = base + xrow0 + kh * g.xp + (kWgPadL + SW * (wo0 + col0) - g.pW) * CI;
+        float win[NWIN2];
+#pragma unroll
+        for (int q = 0; q < NWIN2 / 2; ++q) {
+          const float2 v = *reinterpret_cast<const float2*>(xw + 2 * q);
+          win[2 * q] = v.x;
+          win[2 * q + 1] = v.y;
+        }
+        const float* dsrc = base + (FUSED ? 2 * chunk : 0) + col0 * Co + 4 * cg;
+        float d[kWgWpt][4];
+#pragma unroll
+        for (int j = 0; j < kWgWpt; ++j) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (col0 + j < nv) v = *reinterpret_cast<const float4*>(dsrc + j * Co);
+          d[j][0] = v.x;
+          d[j][1] = v.y;
+          d[j][2] = v.z;
+          d[j][3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < kWgWpt; ++j)
+#pragma unroll
+          for (int k = 0; k < KWC; ++k)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[k][c] = fmaf(win[j * STEP + k], d[j][c], acc[k][c]);
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(&empty[sl]);
+    }
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  __syncthreads();  // every copy has landed (producer drain) and every slot is read
 
   // Fold the teams in team order, one partial per filter element (HWIO).
-  float* fold = body;
+  float* fold = wsm;
+  const bool computes = ct >= 0 && team < g.teams;
   if (computes) {
 #pragma unroll
     for (int k = 0; k < KWC; ++k)
@@ -292,24 +396,47 @@ constexpr int kStemKW = 7, kStemCI = 3, kStemSW = 2;
 
 }  // namespace
 
+namespace {
+
+// The geometry of a launch (the number of ring slots is the largest that fits
+// `max_smem`, at most kWgMaxStages; 0 if not even two fit).
+WgGeom wg_geom(const ConvGeom& g, bool fused, int max_smem) {
+  constexpr int KWC = kStemKW * kStemCI;
+  WgGeom w{};
+  w.N = (int)g.N; w.H = (int)g.H; w.W = (int)g.W; w.Co = (int)g.Co; w.kH = (int)g.kH; w.sH = (int)g.sH;
+  w.pH = (int)g.pH; w.pW = (int)g.pW; w.Ho = (int)g.Ho; w.Wo = (int)g.Wo;
+  w.team = w.kH * w.Co / 4;
+  w.teams = kWgConsumers / w.team;
+  w.Wc = w.teams * kWgWpt;
+  w.chunks = (int)ceil_div(w.Wo, w.Wc);
+  // a window reads up to (padL + sW * (Wo + kWgWpt - 1) + kW) * Ci staged floats
+  w.xp = (int)ceil_div((int64_t)(kWgPadL + kStemSW * (w.Wo + kWgWpt - 1) + kStemKW) * kStemCI, 4) * 4;
+  w.slot = wg_slot_floats(w.Wc, w.Co, w.kH, w.xp, fused);
+  w.stages = 0;
+  for (int st = kWgMaxStages; st >= 2; --st) {
+    w.stages = st;
+    if (wg_smem_bytes<KWC>(w) <= max_smem) break;
+    w.stages = 0;
+  }
+  return w;
+}
+
+}  // namespace
+
 // The shapes this kernel takes: a 7-wide filter over 3 input channels with
-// column stride 2 (the README stem, any batch / image size / filter height up
-// to 8 / output channel count that is a multiple of 4 and fits a team), and a
-// 16-byte aligned output gradient.
-bool conv_wgrad_rows_ok(const ConvGeom& g, const float* dy, const float* ybn) {
+// column stride 2 (the README stem at any batch and image height), image
+// widths that are a multiple of 4 (whole input rows are staged with 16-byte
+// bulk copies), an even left padding (the window loads are 8-byte aligned),
+// 4 to 256 output channels in groups of 4, filter heights up to 8, 16-byte
+// aligned tensors, and a ring of at least two slots in shared memory.
+bool conv_wgrad_rows_ok(const ConvGeom& g, const float* x, const float* dy, const float* ybn) {
   if (g.kW != kStemKW || g.Ci != kStemCI || g.sW != kStemSW) return false;
-  if (g.Co < 4 || g.Co % 4 != 0 || g.kH < 1 || g.kH > 8 || g.N < 1 || g.Ho < 1 || g.Wo < 1) return false;
-  if (g.kH * g.Co / 4 > kWgThreads) return false;
-  if (!aligned16(dy) || (ybn != nullptr && !aligned16(ybn))) return false;
-  const int64_t teams = kWgThreads / (g.kH * g.Co / 4);
-  const int64_t wc = teams * kWgWpt;
-  // shared memory (the fused plan is the larger): 7 constants per channel, the
-  // ring of unit buffers or the team fold, within the 227 KB a CTA may use
-  const int64_t seg = ((wc - 1) * kStemSW + kStemKW) * kStemCI + 8;
-  const int64_t ring = kWgStages * (wc * g.Co * 2 + g.kH * seg);
-  const int64_t fold = kWgThreads * kStemKW * kStemCI * 4;
-  if (4 * (kWgConsts * g.Co + (ring > fold ? ring : fold)) > 227 * 1024) return false;
-  return g.N * g.Ho * ceil_div(g.Wo, wc) <= INT_MAX && g.H <= INT_MAX && g.W <= INT_MAX;
+  if (g.Co < 4 || g.Co > 256 || g.Co % 4 != 0 || g.kH < 1 || g.kH > 8 || g.N < 1 || g.Ho < 1 || g.Wo < 1)
+    return false;
+  if (g.W % 4 != 0 || g.pW % 2 != 0 || g.pW > kWgPadL || g.kH * g.Co / 4 > kWgConsumers) return false;
+  if (!aligned16(x) || !aligned16(dy) || (ybn != nullptr && !aligned16(ybn))) return false;
+  if (g.W > 1 << 20 || g.H > INT_MAX || g.N * g.Ho * g.Wo > INT_MAX) return false;
+  return wg_geom(g, true, 227 * 1024).stages >= 2;
 }
 
 namespace {
@@ -319,28 +446,18 @@ namespace {
 // gradient is the BatchNorm -> ReLU backward of them with these constants.
 int wgrad_rows(const ConvGeom& g, const float* x, const float* dy, const float* ybn, const BnDx* fused, float* dw,
                cudaStream_t s) {
+  constexpr int KWC = kStemKW * kStemCI;
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
-  WgGeom w;
-  w.N = (int)g.N; w.H = (int)g.H; w.W = (int)g.W; w.Co = (int)g.Co; w.kH = (int)g.kH; w.sH = (int)g.sH;
-  w.pH = (int)g.pH; w.pW = (int)g.pW; w.Ho = (int)g.Ho; w.Wo = (int)g.Wo;
-  w.team = w.kH * w.Co / 4;
-  w.teams = kWgThreads / w.team;
-  w.Wc = w.teams * kWgWpt;
-  w.chunks = (int)ceil_div(w.Wo, w.Wc);
-  constexpr int KWC = kStemKW * kStemCI, STEP = kStemSW * kStemCI;
-  constexpr int NWIN4 = ((kWgWpt - 1) * STEP + KWC + 3) / 4 * 4;
-  w.seg_valid = ((w.Wc - 1) * kStemSW + kStemKW) * kStemCI;
-  const int need = (w.teams - 1) * kWgWpt * STEP + NWIN4;  // the last team's window read
-  w.seg = (int)ceil_div(w.seg_valid > need ? w.seg_valid : need, 4) * 4;
+  const bool is_fused = fused != nullptr;
+  WgGeom w = wg_geom(g, is_fused, d->max_smem_optin);
+  B2_REQUIRE(w.stages >= 2, "conv2d_backprop_filter: shared memory too small for this shape");
   w.units = w.N * w.Ho * w.chunks;
   int blocks = w.units < d->sm_count ? w.units : d->sm_count;
   w.upb = (int)ceil_div(w.units, blocks);
   blocks = (int)ceil_div(w.units, w.upb);
-  const bool is_fused = fused != nullptr;
-  const WgSmem plan = wg_smem<KWC>(w, is_fused);
-  const int smem = plan.total * (int)sizeof(float);
-  B2_REQUIRE(smem <= d->max_smem_optin, "conv2d_backprop_filter: %d bytes of shared memory needed", smem);
+  w.wait = wait_params();
+  const int smem = wg_smem_bytes<KWC>(w);
   const int64_t F = g.kH * KWC * g.Co;
   Scratch part;
   B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)blocks * F, s));
@@ -349,12 +466,12 @@ int wgrad_rows(const ConvGeom& g, const float* x, const float* dy, const float* 
     static SmemOptIn opt_in;
     auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, true>;
     B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), d->device, smem));
-    k<<<blocks, kWgThreads, smem, s>>>(x, dy, ybn, bn, w, part.as<float>());
+    k<<<blocks, wg_threads(true), smem, s>>>(x, dy, ybn, bn, w, part.as<float>());
   } else {
     static SmemOptIn opt_in;
     auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, false>;
     B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), d->device, smem));
-    k<<<blocks, kWgThreads, smem, s>>>(x, dy, nullptr, bn, w, part.as<float>());
+    k<<<blocks, wg_threads(false), smem, s>>>(x, dy, nullptr, bn, w, part.as<float>());
   }
   B2_RETURN_IF_ERROR(check_launch(s, is_fused ? "conv2d_bn_relu_backprop_filter" : "conv2d_backprop_filter"));
   wgrad_block_sum_kernel<<<(unsigned)ceil_div(F, 32), dim3(32, kSumParts), 0, s>>>(part.as<float>(), blocks,
@@ -363,6 +480,14 @@ int wgrad_rows(const ConvGeom& g, const float* x, const float* dy, const float* 
 }
 
 }  // namespace
+
+// Expired bounded waits of the stem filter-gradient kernel (read by
+// b2_device_timeouts).
+unsigned int wg_timeouts() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_wg_timeouts, sizeof(v));
+  return v;
+}
 
 int conv_wgrad_rows(const ConvGeom& g, const float* x, const float* dy, float* dw, cudaStream_t s) {
   return wgrad_rows(g, x, dy, nullptr, nullptr, dw, s);
@@ -401,7 +526,7 @@ extern "C" int b2_conv2d_batch_norm_relu_backprop_filter(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows = g.N * g.Ho * g.Wo;
   if (g.Co == 0) return B2_OK;
-  if (conv_direct_ok(g) || !conv_wgrad_rows_ok(g, grad_z, bn_input) || rows == 0) {
+  if (conv_direct_ok(g) || !conv_wgrad_rows_ok(g, input, grad_z, bn_input) || rows == 0) {
     // any shape b2_conv2d_backprop_filter does not give to this kernel: the
     // two ops in sequence, the input gradient in scratch
     Scratch dx;

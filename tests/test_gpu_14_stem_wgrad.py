@@ -4,8 +4,9 @@ fusion with the BatchNorm -> ReLU backward.
 * conv2d_backprop_filter of 7-wide, 3-channel, column-stride-2 filters with
   more than 32 output channels (the README stem: 3x7x3x48 over 64x64 images;
   the widened stem 3x7x3x96 over 256x256) against the oracle (the reference's
-  arithmetic) and float64, with ragged shapes: odd widths, a partial last
-  column chunk, VALID padding, one image row, filter heights 1 and 5;
+  arithmetic) and float64, with ragged shapes: units with unused columns,
+  VALID padding, one image row, filter heights 1 and 5, an odd width that
+  another engine takes;
 * fused_ops.opencl_conv2d_batch_norm_relu_backprop_filter equal bit for bit
   to opencl_batch_norm_relu_grad followed by opencl_conv2d_backprop_filter,
   on the kernel's shapes and on a shape it does not take (the fallback);
@@ -45,11 +46,12 @@ def _wgrad_f64(x, dy, kshape, strides, padding):
 
 CASES = [
     ((8, 64, 64, 3), (3, 7, 3, 48), "SAME"),    # the README stem at a small batch
-    ((2, 9, 37, 3), (3, 7, 3, 48), "SAME"),     # odd width: columns beyond the last output in the chunk
-    ((3, 11, 30, 3), (5, 7, 3, 40), "VALID"),   # VALID, filter height 5, 20-column chunks (a partial one)
+    ((2, 9, 36, 3), (3, 7, 3, 48), "SAME"),     # 18 output columns of a 32-column unit
+    ((3, 11, 28, 3), (5, 7, 3, 40), "VALID"),   # VALID, filter height 5, 20-column units (11 used)
     ((4, 1, 64, 3), (1, 7, 3, 96), "SAME"),     # one image row, filter height 1, 96 channels
     ((3, 5, 64, 3), (3, 7, 3, 96), "SAME"),     # 96 channels: two column chunks per output row
     ((2, 32, 256, 3), (3, 7, 3, 96), "SAME"),   # the widened stem's width and channels
+    ((2, 9, 37, 3), (3, 7, 3, 48), "SAME"),     # odd width: not this kernel's (another engine)
 ]
 
 
@@ -89,13 +91,14 @@ def test_stem_filter_gradient_deterministic(otf):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("xs,ws", [((8, 64, 64, 3), (3, 7, 3, 48)), ((2, 9, 37, 3), (3, 7, 3, 40)),
-                                   ((2, 9, 37, 3), (3, 7, 3, 16)), ((2, 10, 12, 5), (3, 3, 5, 40))])
+@pytest.mark.parametrize("xs,ws", [((8, 64, 64, 3), (3, 7, 3, 48)), ((2, 9, 36, 3), (3, 7, 3, 40)),
+                                   ((2, 9, 37, 3), (3, 7, 3, 48)), ((2, 9, 36, 3), (3, 7, 3, 16)),
+                                   ((2, 10, 12, 5), (3, 3, 5, 40))])
 def test_fused_conv_bn_relu_filter_gradient_equals_the_ops(otf, xs, ws):
     """The fused op against ReluGrad -> BatchNormGrad -> Conv2DBackpropFilter
-    (the last two shapes are not ones the fused kernel takes -- 16 output
-    channels go to the narrow-filter kernel, 5 input channels to the GEMM
-    engines: the fallback)."""
+    (the last three shapes are not ones the fused kernel takes -- an odd
+    width, 16 output channels (the narrow-filter kernel), 5 input channels
+    (the GEMM engines): the fallback)."""
     from opencl_tf import fused_ops, raw_ops
     g = torch.Generator(device="cuda").manual_seed(6)
     x = torch.rand(*xs, device="cuda", generator=g)
