@@ -14,28 +14,29 @@
 // input row) with the Co output-gradient values.  As a GEMM its M = kH*kW*Ci =
 // 63 fills half of a 128-row MMA, and its im2col^T operand has to be
 // transposed element by element by converter warps; here each thread keeps the
-// window in registers instead: a thread owns (kh, 4 output channels) and
-// accumulates 21 x 4 sums over WPT = 4 adjacent output columns, whose windows
-// overlap (stride 2: each column adds 2 pixels), so a column costs 84 FMAs
-// against one 16-byte load of dy and 1.5 of x.
+// window in registers instead: a thread owns (kh, CPT = 3 or 4 output
+// channels) and accumulates 21 x CPT sums over WPT = 4 adjacent output
+// columns, whose windows overlap (stride 2: each column adds 2 pixels).
 //
-// Work unit: one output row (n, ho), or a chunk of Wc of its columns.  A CTA
-// (one per SM) walks a contiguous range of units through a ring of
-// shared-memory slots, with three warp roles and no block-wide barrier:
+// Work unit: R output rows (n, ho..ho+R-1), or, when a row's dy does not fit a
+// slot, a chunk of Wc of one row's columns.  A CTA (one per SM) walks a
+// contiguous range of units through a ring of shared-memory slots with three
+// warp roles and no block-wide barrier:
 //
-//   warp 0        lane 0 stages a unit with 1-D bulk copies (cp.async.bulk,
-//                 completion on the slot's FULL mbarrier): the dy chunk (a
-//                 contiguous span of the NHWC tensor) and the kH whole input
-//                 rows it reads, each placed between zero margins that the
-//                 copies never touch, so every tap of every column lands
-//                 inside the slot; input rows outside the image are flagged;
+//   warp 0        lane 0 stages a unit with two or three 1-D bulk copies
+//                 (cp.async.bulk, completion on the slot's FULL mbarrier): the
+//                 unit's dy block (contiguous in NHWC), FUSED also the BatchNorm
+//                 input block, and the contiguous run of input rows the unit
+//                 reads (clipped to the image); its unit bookkeeping is
+//                 incremental, without divisions, so it keeps ahead;
 //   warps 1..2    (FUSED) compute dy = the BatchNorm -> ReLU backward of the
 //                 staged dz and y, with the per-channel constants in
 //                 registers, into the slot, and arrive on DX_READY;
-//   warps 3..     consumers: teams of kH * Co/4 threads split the unit's
-//                 columns; each thread loads its input window (kW*Ci + 3*sW*Ci
-//                 floats) and its 4 x 4 dy values and issues the FMAs, then
-//                 its warp arrives on EMPTY.
+//   12 warps      consumers, three per scheduler: teams of kH * Co/CPT threads
+//                 split the unit's column groups; a thread loads its input
+//                 window (input columns outside the image read as zero), its
+//                 WPT x CPT dy values and issues the FMAs; each warp arrives on
+//                 EMPTY.
 //
 // Every wait is bounded.  At the end the CTA folds its teams in team order
 // and writes one partial per filter element; a second kernel adds the CTA
@@ -57,27 +58,31 @@ static __device__ unsigned int g_wg_timeouts = 0;
 
 namespace {
 
-constexpr int kWgConsumers = 288;  // 9 consumer warps
-constexpr int kWgDxWarps = 2;      // FUSED: dx warps
-constexpr int kWgWpt = 4;          // output columns per consumer thread per unit
-constexpr int kWgMaxStages = 6;
-constexpr int kWgPadL = 4;         // zero pixels staged before each input row
+constexpr int kWgConsumerWarps = 12;  // three per scheduler
+constexpr int kWgConsumers = 32 * kWgConsumerWarps;
+constexpr int kWgDxWarps = 2;         // FUSED: dx warps
+constexpr int kWgWpt = 4;             // output columns per consumer thread per group
+constexpr int kWgMaxStages = 8;
+constexpr int kWgMargin = 64;         // floats before / after the staged input rows
+constexpr int kWgSlotBudget = 40 * 1024;  // target bytes of one slot
 
 __host__ __device__ constexpr int wg_threads(bool fused) {
-  return 32 * (1 + (fused ? kWgDxWarps : 0) + kWgConsumers / 32);
+  return 32 * (1 + (fused ? kWgDxWarps : 0) + kWgConsumerWarps);
 }
 
 struct WgGeom {
   int N, H, W, Co, kH, sH, pH, pW, Ho, Wo;
-  int teams;   // consumer teams
-  int team;    // threads per team: kH * Co / 4
-  int Wc;      // output columns per unit: teams * kWgWpt
-  int chunks;  // units per output row
-  int xp;      // staged floats per input row: zero margin, W*Ci values, zero margin (multiple of 4)
-  int slot;    // floats per slot
-  int stages;  // slots
-  int units;   // N * Ho * chunks
-  int upb;     // units per CTA
+  int cpt;      // output channels per consumer thread (3 or 4)
+  int combos;   // threads per team: kH * Co / cpt
+  int teams;    // consumer teams
+  int R;        // output rows per unit (1 when chunks > 1)
+  int Wc;       // output columns per unit (Wo when chunks == 1)
+  int chunks;   // units per block of R rows
+  int xrows;    // input rows staged per unit: (R - 1) * sH + kH
+  int slot;     // floats per slot
+  int stages;   // slots
+  int units;    // (N * Ho / R) * chunks
+  int upb;      // units per CTA
   WaitParams wait;
 };
 
@@ -151,47 +156,72 @@ __device__ __forceinline__ void bulk_g2s(float* dst, const float* src, uint32_t 
                : "memory");
 }
 
-// Slot layout (floats): dy (or dz) chunk [Wc][Co]; FUSED: BN-input chunk
-// [Wc][Co] and the computed dy chunk [Wc][Co]; then kH input rows [xp].
-__host__ __device__ inline int wg_slot_floats(int Wc, int Co, int kH, int xp, bool fused) {
-  return Wc * Co * (fused ? 3 : 1) + kH * xp;
+// Where a unit is: output rows ho .. ho + R - 1 of image n, columns wo0 ..
+// wo0 + Wc - 1; advanced one unit at a time without dividing.
+struct UnitPos {
+  int n, ho, c;
+  __device__ void start(const WgGeom& g, int u) {
+    const int rb = u / g.chunks;
+    c = u - rb * g.chunks;
+    const int row = rb * g.R;
+    n = row / g.Ho;
+    ho = row - n * g.Ho;
+  }
+  __device__ void next(const WgGeom& g) {
+    if (++c == g.chunks) {
+      c = 0;
+      ho += g.R;
+      if (ho == g.Ho) {
+        ho = 0;
+        ++n;
+      }
+    }
+  }
+};
+
+// Slot layout (floats): dy (or dz) block [R][Wc][Co]; FUSED: BN-input block
+// and the computed dy block, same shape; then kWgMargin, the input rows
+// [xrows][W*Ci], kWgMargin.
+__host__ __device__ inline int wg_block(const WgGeom& g) { return g.R * g.Wc * g.Co; }
+__host__ __device__ inline int wg_xoff(const WgGeom& g, bool fused) {
+  return wg_block(g) * (fused ? 3 : 1) + kWgMargin;
+}
+__host__ __device__ inline int wg_slot_floats(const WgGeom& g, bool fused) {
+  return wg_xoff(g, fused) + g.xrows * g.W * 3 + kWgMargin;
 }
 
-// Dynamic shared memory: max(ring, team fold) + barriers and row flags.
+// Dynamic shared memory: max(ring, team fold) + barriers.
 template <int KWC>
 __host__ __device__ inline int wg_smem_bytes(const WgGeom& g) {
   const int ring = g.stages * g.slot;
-  const int fold = g.teams * g.team * KWC * 4;
+  const int fold = g.teams * g.combos * KWC * g.cpt;
   const int body = (ring > fold ? ring : fold) * 4;
-  return body + 8 * 3 * kWgMaxStages + 4 * kWgMaxStages * 8 + 16;
+  return body + 8 * 3 * kWgMaxStages + 16;
 }
 
-template <int KW, int CI, int SW, bool FUSED>
+template <int KW, int CI, int SW, int CPT, bool FUSED>
 __global__ void __launch_bounds__(wg_threads(FUSED), 1)
     conv_wgrad_rows_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                            const float* __restrict__ ybn, BnDx bn, WgGeom g, float* __restrict__ partial) {
   constexpr int KWC = KW * CI;
   constexpr int STEP = SW * CI;                    // window shift per output column
   constexpr int NWIN = (kWgWpt - 1) * STEP + KWC;  // floats of x a thread's columns read per filter row
-  constexpr int NWIN2 = (NWIN + 1) / 2 * 2;
   constexpr int kConsumer0 = 32 * (1 + (FUSED ? kWgDxWarps : 0));
   extern __shared__ __align__(16) float wsm[];
-  const int S = g.stages, Co = g.Co, cq = Co / 4, chunk = g.Wc * Co;
-  const int fold_floats = g.teams * g.team * KWC * 4;
+  const int S = g.stages, Co = g.Co, blk = wg_block(g), xoff = wg_xoff(g, FUSED), WCI = g.W * CI;
+  const int fold_floats = g.teams * g.combos * KWC * CPT;
   const int body = S * g.slot > fold_floats ? S * g.slot : fold_floats;
   uint64_t* full = reinterpret_cast<uint64_t*>(wsm + body);
   uint64_t* dxr = full + kWgMaxStages;
   uint64_t* empty = dxr + kWgMaxStages;
-  int* rowok = reinterpret_cast<int*>(empty + kWgMaxStages);  // [S][kH]
   __shared__ int s_abort;
   volatile int* abort = &s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int u_begin = blockIdx.x * g.upb;
   const int nu = (u_begin + g.upb < g.units ? u_begin + g.upb : g.units) - u_begin;
-  const int consumer_warps = (g.teams * g.team + 31) / 32;
 
-  // zero the ring once: the input rows' margins are never written again
+  // the margins around the input rows are never written by the copies
   for (int i = tid; i < S * g.slot; i += blockDim.x) wsm[i] = 0.0f;
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (tid == 0) {
@@ -199,50 +229,45 @@ __global__ void __launch_bounds__(wg_threads(FUSED), 1)
     for (int i = 0; i < S; ++i) {
       bar_init(&full[i], 1);
       bar_init(&dxr[i], kWgDxWarps);
-      bar_init(&empty[i], consumer_warps);
+      bar_init(&empty[i], kWgConsumerWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  const int xrow0 = chunk * (FUSED ? 3 : 1);  // offset of the input rows in a slot
-  float acc[KWC][4];
+  float acc[KWC][CPT];
 #pragma unroll
-  for (int k = 0; k < KWC; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
+  for (int k = 0; k < KWC; ++k)
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[k][c] = 0.0f;
   const int ct = tid - kConsumer0;
-  const int team = ct >= 0 ? ct / g.team : g.teams, r = ct >= 0 ? ct - team * g.team : 0;
-  const int kh = r / cq, cg = r - kh * cq;
+  const int ng = g.Co / CPT;  // channel groups
+  const int team = ct >= 0 ? ct / g.combos : g.teams, r = ct >= 0 ? ct - team * g.combos : 0;
+  const int kh = r / ng, cgrp = r - kh * ng;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int issued = 0;
-      for (int i = 0; i < nu; ++i, ++issued) {
+      UnitPos up;
+      up.start(g, u_begin);
+      for (int i = 0; i < nu; ++i, ++issued, up.next(g)) {
         const int sl = i % S;
         if (i >= S && !bar_wait(&empty[sl], (uint32_t)(i / S - 1) & 1u, g.wait, abort)) break;
-        const int u = u_begin + i;
-        const int row = u / g.chunks, c = u - row * g.chunks;
-        const int n = row / g.Ho, ho = row - n * g.Ho;
-        const int wo0 = c * g.Wc;
-        const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
         float* base = wsm + (size_t)sl * g.slot;
-        uint32_t bytes = (uint32_t)(nv * Co * 4) * (FUSED ? 2u : 1u);
-        for (int k = 0; k < g.kH; ++k) {
-          const int hi = ho * g.sH - g.pH + k;
-          const bool ok = hi >= 0 && hi < g.H;
-          rowok[sl * g.kH + k] = ok;
-          if (ok) bytes += (uint32_t)(g.W * CI * 4);
-        }
-        bar_expect_tx(&full[sl], bytes);
-        const int64_t d0 = ((int64_t)row * g.Wo + wo0) * Co;
-        bulk_g2s(base, dy + d0, (uint32_t)(nv * Co * 4), &full[sl]);
-        if (FUSED) bulk_g2s(base + chunk, ybn + d0, (uint32_t)(nv * Co * 4), &full[sl]);
-        for (int k = 0; k < g.kH; ++k) {
-          const int hi = ho * g.sH - g.pH + k;
-          if (hi >= 0 && hi < g.H)
-            bulk_g2s(base + xrow0 + k * g.xp + kWgPadL * CI, x + ((int64_t)n * g.H + hi) * g.W * CI,
-                     (uint32_t)(g.W * CI * 4), &full[sl]);
-        }
+        const int wo0 = up.c * g.Wc;
+        const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
+        // input rows (R - 1) * sH + kH from ho * sH - pH, clipped to the image
+        int h0 = up.ho * g.sH - g.pH, h1 = h0 + g.xrows;
+        const int c0 = h0 < 0 ? 0 : h0, c1 = h1 > g.H ? g.H : h1;
+        const uint32_t dbytes = (uint32_t)(g.R * nv * Co * 4);
+        const uint32_t xbytes = c1 > c0 ? (uint32_t)((c1 - c0) * WCI * 4) : 0u;
+        bar_expect_tx(&full[sl], dbytes * (FUSED ? 2u : 1u) + xbytes);
+        const int64_t d0 = (((int64_t)up.n * g.Ho + up.ho) * g.Wo + wo0) * Co;
+        bulk_g2s(base, dy + d0, dbytes, &full[sl]);
+        if (FUSED) bulk_g2s(base + blk, ybn + d0, dbytes, &full[sl]);
+        if (xbytes)
+          bulk_g2s(base + xoff + (c0 - h0) * WCI, x + ((int64_t)up.n * g.H + c0) * WCI, xbytes, &full[sl]);
       }
       // let every issued copy land before the CTA can leave its ring
       const int first = issued > S ? issued - S : 0;
@@ -254,14 +279,15 @@ __global__ void __launch_bounds__(wg_threads(FUSED), 1)
     }
   } else if (FUSED && warp <= kWgDxWarps) {
     // ------------------------------------------------------- dx (FUSED)
-    // thread t: channel group t % cq of rows t / cq, t / cq + lanes_per, ...
+    // thread t: channel quad t % cq of columns t / cq, t / cq + per, ...
+    const int cq = Co / 4;
     const int t = tid - 32, per = (32 * kWgDxWarps) / cq;
     const bool active = t < per * cq;
-    const int dcg = active ? t % cq : 0, wl0 = t / cq;
+    const int dcq = active ? t % cq : 0, wl0 = t / cq;
     float m[4], iv[4], k1[4], gb[4], gg[4], ga[4], be[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int ch = 4 * dcg + j;
+      const int ch = 4 * dcq + j;
       m[j] = bn.mean[ch];
       iv[j] = bn.inv_std[ch];
       k1[j] = bn.k1[ch];
@@ -270,71 +296,98 @@ __global__ void __launch_bounds__(wg_threads(FUSED), 1)
       ga[j] = bn.gamma[ch];
       be[j] = bn.beta[ch];
     }
-    for (int i = 0; i < nu; ++i) {
+    UnitPos up;
+    up.start(g, u_begin);
+    for (int i = 0; i < nu; ++i, up.next(g)) {
       const int sl = i % S;
       if (!bar_wait(&full[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
-      const int u = u_begin + i;
-      const int wo0 = (u - (u / g.chunks) * g.chunks) * g.Wc;
+      const int wo0 = up.c * g.Wc;
       const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
       float* base = wsm + (size_t)sl * g.slot;
       if (active) {
-        for (int wl = wl0; wl < nv; wl += per) {
-          const int e = wl * Co + 4 * dcg;
-          const float4 z4 = *reinterpret_cast<const float4*>(base + e);
-          const float4 y4 = *reinterpret_cast<const float4*>(base + chunk + e);
-          float4 o;
-          o.x = bn_grad_dx_value<true>(y4.x, z4.x, m[0], iv[0], k1[0], gb[0], gg[0], ga[0], be[0], bn.nhw_f);
-          o.y = bn_grad_dx_value<true>(y4.y, z4.y, m[1], iv[1], k1[1], gb[1], gg[1], ga[1], be[1], bn.nhw_f);
-          o.z = bn_grad_dx_value<true>(y4.z, z4.z, m[2], iv[2], k1[2], gb[2], gg[2], ga[2], be[2], bn.nhw_f);
-          o.w = bn_grad_dx_value<true>(y4.w, z4.w, m[3], iv[3], k1[3], gb[3], gg[3], ga[3], be[3], bn.nhw_f);
-          *reinterpret_cast<float4*>(base + 2 * chunk + e) = o;
+        for (int rr = 0; rr < g.R; ++rr) {
+#pragma unroll 2
+          for (int wl = wl0; wl < nv; wl += per) {
+            const int e = (rr * g.Wc + wl) * Co + 4 * dcq;
+            const float4 z4 = *reinterpret_cast<const float4*>(base + e);
+            const float4 y4 = *reinterpret_cast<const float4*>(base + blk + e);
+            float4 o;
+            o.x = bn_grad_dx_value<true>(y4.x, z4.x, m[0], iv[0], k1[0], gb[0], gg[0], ga[0], be[0], bn.nhw_f);
+            o.y = bn_grad_dx_value<true>(y4.y, z4.y, m[1], iv[1], k1[1], gb[1], gg[1], ga[1], be[1], bn.nhw_f);
+            o.z = bn_grad_dx_value<true>(y4.z, z4.z, m[2], iv[2], k1[2], gb[2], gg[2], ga[2], be[2], bn.nhw_f);
+            o.w = bn_grad_dx_value<true>(y4.w, z4.w, m[3], iv[3], k1[3], gb[3], gg[3], ga[3], be[3], bn.nhw_f);
+            *reinterpret_cast<float4*>(base + 2 * blk + e) = o;
+          }
         }
       }
       __syncwarp();
       if (lane == 0) bar_arrive(&dxr[sl]);
     }
-  } else if (ct >= 0 && ct < consumer_warps * 32) {
+  } else if (ct >= 0) {
     // ----------------------------------------------------------- consumers
     const bool active = team < g.teams;
-    for (int i = 0; i < nu; ++i) {
+    const int groups = (g.Wc + kWgWpt - 1) / kWgWpt;  // column groups of a unit row
+    UnitPos up;
+    up.start(g, u_begin);
+    for (int i = 0; i < nu; ++i, up.next(g)) {
       const int sl = i % S;
-      // FULL (the staged input rows: completed before DX_READY, so this returns
-      // at once in the fused kernel, but it makes the bulk copies' writes
+      // FULL (the staged input rows; in the fused kernel it has completed
+      // before DX_READY, but waiting on it makes the bulk copies' writes
       // visible to this thread directly) then, fused, DX_READY
       if (!bar_wait(&full[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
       if (FUSED && !bar_wait(&dxr[sl], (uint32_t)(i / S) & 1u, g.wait, abort)) break;
-      const int u = u_begin + i;
-      const int wo0 = (u - (u / g.chunks) * g.chunks) * g.Wc;
+      const int wo0 = up.c * g.Wc;
       const int nv = g.Wo - wo0 < g.Wc ? g.Wo - wo0 : g.Wc;
-      const int col0 = team * kWgWpt;  // first column of this team in the unit
       const float* base = wsm + (size_t)sl * g.slot;
-      if (active && col0 < nv && rowok[sl * g.kH + kh]) {
-        // window: staged position (padL + sW * (wo0 + col0) - pW) * Ci of row kh
-        const float* xw = base + xrow0 + kh * g.xp + (kWgPadL + SW * (wo0 + col0) - g.pW) * CI;
-        float win[NWIN2];
+      const float* dsrc0 = base + (FUSED ? 2 * blk : 0) + CPT * cgrp;
+      const int h_base = up.ho * g.sH - g.pH;  // first staged input row (may be outside the image)
+      if (active) {
+        for (int rr = 0; rr < g.R; ++rr) {
+          const int hi = h_base + rr * g.sH + kh;
+          if (hi < 0 || hi >= g.H) continue;  // a zero-padding row contributes nothing
+          const float* xrow = base + xoff + (hi - h_base) * WCI;  // staged row hi - h_base
+          for (int gi = team; gi < groups; gi += g.teams) {
+            const int col0 = gi * kWgWpt;
+            if (col0 >= nv) break;
+            const int cin0 = SW * (wo0 + col0) - g.pW;  // input column of window entry 0
+            const float* xw = xrow + cin0 * CI;
+            // at the image edge, input columns outside it read as zero (SAME padding)
+            const bool edge = cin0 < 0 || cin0 + (NWIN - 1) / CI >= g.W;
+            auto ld = [&](int q) {
+              float v = xw[q];
+              if (edge) {
+                const int cc = cin0 + q / CI;
+                if (cc < 0 || cc >= g.W) v = 0.0f;
+              }
+              return v;
+            };
+            const float* ds = dsrc0 + (rr * g.Wc + col0) * Co;
+            float d[kWgWpt][CPT];
 #pragma unroll
-        for (int q = 0; q < NWIN2 / 2; ++q) {
-          const float2 v = *reinterpret_cast<const float2*>(xw + 2 * q);
-          win[2 * q] = v.x;
-          win[2 * q + 1] = v.y;
+            for (int j = 0; j < kWgWpt; ++j) {
+              const bool ok = col0 + j < nv;
+#pragma unroll
+              for (int c = 0; c < CPT; ++c) d[j][c] = ok ? ds[j * Co + c] : 0.0f;
+            }
+            // a rolling window of KWC + STEP floats: column j reads entries
+            // j*STEP .. j*STEP + KWC - 1, entry q kept at q % NRING
+            constexpr int NRING = KWC + STEP;
+            float win[NRING];
+#pragma unroll
+            for (int q = 0; q < KWC; ++q) win[q] = ld(q);
+#pragma unroll
+            for (int j = 0; j < kWgWpt; ++j) {
+              if (j > 0) {
+#pragma unroll
+                for (int t = 0; t < STEP; ++t) win[(j * STEP + KWC - STEP + t) % NRING] = ld(j * STEP + KWC - STEP + t);
+              }
+#pragma unroll
+              for (int k = 0; k < KWC; ++k)
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) acc[k][c] = fmaf(win[(j * STEP + k) % NRING], d[j][c], acc[k][c]);
+            }
+          }
         }
-        const float* dsrc = base + (FUSED ? 2 * chunk : 0) + col0 * Co + 4 * cg;
-        float d[kWgWpt][4];
-#pragma unroll
-        for (int j = 0; j < kWgWpt; ++j) {
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (col0 + j < nv) v = *reinterpret_cast<const float4*>(dsrc + j * Co);
-          d[j][0] = v.x;
-          d[j][1] = v.y;
-          d[j][2] = v.z;
-          d[j][3] = v.w;
-        }
-#pragma unroll
-        for (int j = 0; j < kWgWpt; ++j)
-#pragma unroll
-          for (int k = 0; k < KWC; ++k)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[k][c] = fmaf(win[j * STEP + k], d[j][c], acc[k][c]);
       }
       __syncwarp();
       if (lane == 0) bar_arrive(&empty[sl]);
@@ -348,8 +401,8 @@ __global__ void __launch_bounds__(wg_threads(FUSED), 1)
   if (computes) {
 #pragma unroll
     for (int k = 0; k < KWC; ++k)
-      *reinterpret_cast<float4*>(fold + ((size_t)(team * g.team + r) * KWC + k) * 4) =
-          make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) fold[((size_t)(team * g.combos + r) * KWC + k) * CPT + c] = acc[k][c];
   }
   __syncthreads();
   if (computes && team == 0) {
@@ -357,15 +410,14 @@ __global__ void __launch_bounds__(wg_threads(FUSED), 1)
     float* out = partial + (int64_t)blockIdx.x * F;
 #pragma unroll 1
     for (int k = 0; k < KWC; ++k) {
-      float4 s = *reinterpret_cast<const float4*>(fold + ((size_t)r * KWC + k) * 4);
-      for (int t = 1; t < g.teams; ++t) {
-        const float4 v = *reinterpret_cast<const float4*>(fold + ((size_t)(t * g.team + r) * KWC + k) * 4);
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
-      *reinterpret_cast<float4*>(out + ((int64_t)kh * KWC + k) * Co + 4 * cg) = s;
+      float sum[CPT];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) sum[c] = fold[((size_t)r * KWC + k) * CPT + c];
+      for (int t = 1; t < g.teams; ++t)
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) sum[c] += fold[((size_t)(t * g.combos + r) * KWC + k) * CPT + c];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) out[((int64_t)kh * KWC + k) * Co + CPT * cgrp + c] = sum[c];
     }
   }
 }
@@ -394,26 +446,38 @@ __global__ void __launch_bounds__(32 * kSumParts)
 
 constexpr int kStemKW = 7, kStemCI = 3, kStemSW = 2;
 
-}  // namespace
-
-namespace {
-
-// The geometry of a launch (the number of ring slots is the largest that fits
-// `max_smem`, at most kWgMaxStages; 0 if not even two fit).
+// The geometry of a launch: units of R rows (or column chunks of one row)
+// whose slot fits kWgSlotBudget where possible, and the largest ring (at most
+// kWgMaxStages slots) that fits `max_smem`; stages = 0 if not even three fit.
 WgGeom wg_geom(const ConvGeom& g, bool fused, int max_smem) {
   constexpr int KWC = kStemKW * kStemCI;
   WgGeom w{};
   w.N = (int)g.N; w.H = (int)g.H; w.W = (int)g.W; w.Co = (int)g.Co; w.kH = (int)g.kH; w.sH = (int)g.sH;
   w.pH = (int)g.pH; w.pW = (int)g.pW; w.Ho = (int)g.Ho; w.Wo = (int)g.Wo;
-  w.team = w.kH * w.Co / 4;
-  w.teams = kWgConsumers / w.team;
-  w.Wc = w.teams * kWgWpt;
-  w.chunks = (int)ceil_div(w.Wo, w.Wc);
-  // a window reads up to (padL + sW * (Wo + kWgWpt - 1) + kW) * Ci staged floats
-  w.xp = (int)ceil_div((int64_t)(kWgPadL + kStemSW * (w.Wo + kWgWpt - 1) + kStemKW) * kStemCI, 4) * 4;
-  w.slot = wg_slot_floats(w.Wc, w.Co, w.kH, w.xp, fused);
+  w.cpt = (w.Co % 3 == 0 && w.kH * (w.Co / 3) <= kWgConsumers) ? 3 : 4;
+  w.combos = w.kH * (w.Co / w.cpt);
+  w.teams = kWgConsumers / w.combos;
+  const int per_col = w.Co * 4 * (fused ? 3 : 1);  // slot bytes of one output column
+  w.R = 1;
+  if ((int64_t)w.Wo * per_col <= kWgSlotBudget) {
+    w.Wc = w.Wo;
+    w.chunks = 1;
+    for (int r = 4; r >= 2; r /= 2)
+      if (w.Ho % r == 0 && (int64_t)r * w.Wo * per_col <= kWgSlotBudget) {
+        w.R = r;
+        break;
+      }
+  } else {
+    const int unit = w.teams * kWgWpt;  // one column group per team
+    int wc = kWgSlotBudget / per_col / unit * unit;
+    if (wc < unit) wc = unit;
+    w.Wc = wc;
+    w.chunks = (int)ceil_div(w.Wo, wc);
+  }
+  w.xrows = (w.R - 1) * w.sH + w.kH;
+  w.slot = (wg_slot_floats(w, fused) + 3) / 4 * 4;
   w.stages = 0;
-  for (int st = kWgMaxStages; st >= 2; --st) {
+  for (int st = kWgMaxStages; st >= 3; --st) {
     w.stages = st;
     if (wg_smem_bytes<KWC>(w) <= max_smem) break;
     w.stages = 0;
@@ -425,21 +489,39 @@ WgGeom wg_geom(const ConvGeom& g, bool fused, int max_smem) {
 
 // The shapes this kernel takes: a 7-wide filter over 3 input channels with
 // column stride 2 (the README stem at any batch and image height), image
-// widths that are a multiple of 4 (whole input rows are staged with 16-byte
-// bulk copies), an even left padding (the window loads are 8-byte aligned),
-// 4 to 256 output channels in groups of 4, filter heights up to 8, 16-byte
-// aligned tensors, and a ring of at least two slots in shared memory.
+// widths that are a multiple of 4 (input rows are staged with 16-byte bulk
+// copies), an even left padding (the window loads are 8-byte aligned), output
+// channel counts that are multiples of 4 up to 256, filter heights up to 8,
+// 16-byte aligned tensors, and a ring of at least three slots in shared
+// memory.
 bool conv_wgrad_rows_ok(const ConvGeom& g, const float* x, const float* dy, const float* ybn) {
   if (g.kW != kStemKW || g.Ci != kStemCI || g.sW != kStemSW) return false;
   if (g.Co < 4 || g.Co > 256 || g.Co % 4 != 0 || g.kH < 1 || g.kH > 8 || g.N < 1 || g.Ho < 1 || g.Wo < 1)
     return false;
-  if (g.W % 4 != 0 || g.pW % 2 != 0 || g.pW > kWgPadL || g.kH * g.Co / 4 > kWgConsumers) return false;
+  if (g.W % 4 != 0 || g.pW % 2 != 0 || g.kH * g.Co / 4 > kWgConsumers) return false;
   if (!aligned16(x) || !aligned16(dy) || (ybn != nullptr && !aligned16(ybn))) return false;
-  if (g.W > 1 << 20 || g.H > INT_MAX || g.N * g.Ho * g.Wo > INT_MAX) return false;
-  return wg_geom(g, true, 227 * 1024).stages >= 2;
+  if (g.W > 1 << 16 || g.H > 1 << 20 || g.N * g.Ho * g.Wo > INT_MAX || g.N * g.H * g.W * 3 > INT_MAX) return false;
+  return wg_geom(g, true, 227 * 1024).stages >= 3;
 }
 
 namespace {
+
+template <int CPT>
+int launch_wgrad_rows(const WgGeom& w, int blocks, int smem, const float* x, const float* dy, const float* ybn,
+                      const BnDx* fused, float* part, int device, cudaStream_t s) {
+  if (fused) {
+    static SmemOptIn opt_in;
+    auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, CPT, true>;
+    B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), device, smem));
+    k<<<blocks, wg_threads(true), smem, s>>>(x, dy, ybn, *fused, w, part);
+  } else {
+    static SmemOptIn opt_in;
+    auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, CPT, false>;
+    B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), device, smem));
+    k<<<blocks, wg_threads(false), smem, s>>>(x, dy, nullptr, BnDx{}, w, part);
+  }
+  return check_launch(s, fused ? "conv2d_bn_relu_backprop_filter" : "conv2d_backprop_filter");
+}
 
 // dW for a shape conv_wgrad_rows_ok accepts.  fused != nullptr: `dy` is the
 // ReLU-output gradient dz and `ybn` the BatchNorm input, and the output
@@ -449,10 +531,9 @@ int wgrad_rows(const ConvGeom& g, const float* x, const float* dy, const float* 
   constexpr int KWC = kStemKW * kStemCI;
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
-  const bool is_fused = fused != nullptr;
-  WgGeom w = wg_geom(g, is_fused, d->max_smem_optin);
-  B2_REQUIRE(w.stages >= 2, "conv2d_backprop_filter: shared memory too small for this shape");
-  w.units = w.N * w.Ho * w.chunks;
+  WgGeom w = wg_geom(g, fused != nullptr, d->max_smem_optin);
+  B2_REQUIRE(w.stages >= 3, "conv2d_backprop_filter: shared memory too small for this shape");
+  w.units = (w.N * w.Ho / w.R) * w.chunks;
   int blocks = w.units < d->sm_count ? w.units : d->sm_count;
   w.upb = (int)ceil_div(w.units, blocks);
   blocks = (int)ceil_div(w.units, w.upb);
@@ -461,19 +542,10 @@ int wgrad_rows(const ConvGeom& g, const float* x, const float* dy, const float* 
   const int64_t F = g.kH * KWC * g.Co;
   Scratch part;
   B2_RETURN_IF_ERROR(part.alloc(sizeof(float) * (size_t)blocks * F, s));
-  const BnDx bn = is_fused ? *fused : BnDx{};
-  if (is_fused) {
-    static SmemOptIn opt_in;
-    auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, true>;
-    B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), d->device, smem));
-    k<<<blocks, wg_threads(true), smem, s>>>(x, dy, ybn, bn, w, part.as<float>());
-  } else {
-    static SmemOptIn opt_in;
-    auto k = conv_wgrad_rows_kernel<kStemKW, kStemCI, kStemSW, false>;
-    B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(k), d->device, smem));
-    k<<<blocks, wg_threads(false), smem, s>>>(x, dy, nullptr, bn, w, part.as<float>());
-  }
-  B2_RETURN_IF_ERROR(check_launch(s, is_fused ? "conv2d_bn_relu_backprop_filter" : "conv2d_backprop_filter"));
+  if (w.cpt == 3)
+    B2_RETURN_IF_ERROR(launch_wgrad_rows<3>(w, blocks, smem, x, dy, ybn, fused, part.as<float>(), d->device, s));
+  else
+    B2_RETURN_IF_ERROR(launch_wgrad_rows<4>(w, blocks, smem, x, dy, ybn, fused, part.as<float>(), d->device, s));
   wgrad_block_sum_kernel<<<(unsigned)ceil_div(F, 32), dim3(32, kSumParts), 0, s>>>(part.as<float>(), blocks,
                                                                                    (int)F, dw);
   return check_launch(s, "conv2d_backprop_filter_sum");
