@@ -447,8 +447,9 @@ __global__ void __launch_bounds__(32 * kSumParts)
 constexpr int kStemKW = 7, kStemCI = 3, kStemSW = 2;
 
 // The geometry of a launch: units of R rows (or column chunks of one row)
-// whose slot fits kWgSlotBudget where possible, and the largest ring (at most
-// kWgMaxStages slots) that fits `max_smem`; stages = 0 if not even three fit.
+// whose fused slot fits kWgSlotBudget where possible, and the largest ring (at
+// most kWgMaxStages slots) that fits `max_smem`; stages = 0 if not even three
+// fit.
 WgGeom wg_geom(const ConvGeom& g, bool fused, int max_smem) {
   constexpr int KWC = kStemKW * kStemCI;
   WgGeom w{};
@@ -457,7 +458,10 @@ WgGeom wg_geom(const ConvGeom& g, bool fused, int max_smem) {
   w.cpt = (w.Co % 3 == 0 && w.kH * (w.Co / 3) <= kWgConsumers) ? 3 : 4;
   w.combos = w.kH * (w.Co / w.cpt);
   w.teams = kWgConsumers / w.combos;
-  const int per_col = w.Co * 4 * (fused ? 3 : 1);  // slot bytes of one output column
+  // slot bytes of one output column, sized for the fused kernel in both: the
+  // unit shape fixes the order of the additions, and the fused and plain
+  // kernels must add in the same order (their results agree bit for bit)
+  const int per_col = w.Co * 4 * 3;
   w.R = 1;
   if ((int64_t)w.Wo * per_col <= kWgSlotBudget) {
     w.Wc = w.Wo;
