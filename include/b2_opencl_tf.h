@@ -276,25 +276,6 @@ int b2_batch_norm_grad(b2_stream_t stream, const float* grad_y,
                        float epsilon, float* grad_x, float* grad_gamma,
                        float* grad_beta);
 
-/* The stem's backward when its input needs no gradient: given z =
- * relu(BN(y)), y = Conv2D(input, filter) as OpenclConv2d,
- * OpenclBatchNormTraining and OpenclRelu compute them, the ReLU and
- * BatchNorm gradients followed by the filter gradient
- * (src/ops/relu_ops.cc:101-165, src/ops/batchnorm_ops.cc:288-422,
- * src/ops/conv2d_ops.cc:328-448), with the BatchNorm input gradient computed
- * where the filter gradient reads it and never written to memory.  grad_z and
- * bn_input (= y) have out_shape; gamma, beta, saved_mean, saved_var,
- * grad_gamma and grad_beta have out_shape[3] elements.  Every output equals
- * b2_batch_norm_relu_grad then b2_conv2d_backprop_filter bit for bit.  Not
- * an op of the reference: the fusion of the pair its layers chain. */
-int b2_conv2d_batch_norm_relu_backprop_filter(
-    b2_stream_t stream, const float* input, const int64_t input_shape[4],
-    const int32_t filter_sizes[4], const float* grad_z, const float* bn_input,
-    const int64_t out_shape[4], const float* gamma, const float* beta,
-    const float* saved_mean, const float* saved_var, float epsilon,
-    const int32_t* strides, int num_strides, const char* padding,
-    float* grad_filter, float* grad_gamma, float* grad_beta);
-
 /* --------------------------------------------------------------- Dense */
 
 /* OpenclDense(x, w, b) -> y = b + x . W -- src/ops/dense_ops.cc:57-146 */

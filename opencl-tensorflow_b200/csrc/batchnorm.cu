@@ -22,7 +22,6 @@
 #include <mutex>
 
 #include "b2_internal.cuh"
-#include "bn_common.cuh"
 
 namespace b2 {
 namespace {
@@ -76,6 +75,12 @@ struct VecT<4> {
   }
   __device__ static void from(const float* o, T* p) { *p = make_float4(o[0], o[1], o[2], o[3]); }
 };
+
+// y of the forward normalisation (batchnorm_kernels.cl:77-80), operation for
+// operation, so a ReLU mask recomputed from it matches the forward's.
+__device__ __forceinline__ float bn_y(float x, float m, float iv, float g, float b) {
+  return __fadd_rn(__fmul_rn(g, __fmul_rn(__fsub_rn(x, m), iv)), b);
+}
 
 // Stage 1.  MODE 0: (sum x, sum x^2).  MODE 1: (sum dy, sum dy * x_hat) with
 // x_hat = (x - mean) * inv_std, inv_std = 1/sqrt(var + eps) per channel.
@@ -403,8 +408,14 @@ __global__ void __launch_bounds__(kThreads)
   }
   auto one = [&](const float* vx, const float* vgz, float* o) {
 #pragma unroll
-    for (int j = 0; j < VEC; ++j)
-      o[j] = bn_grad_dx_value<RELU>(vx[j], vgz[j], m[j], iv[j], kk[j], db[j], dg[j], gm[j], bt[j], nhw_f);
+    for (int j = 0; j < VEC; ++j) {
+      const float xh = __fmul_rn(__fsub_rn(vx[j], m[j]), iv[j]);
+      const float gv = RELU && !(__fadd_rn(__fmul_rn(gm[j], xh), bt[j]) > 0.0f) ? 0.0f : vgz[j];
+      float t = __fmul_rn(nhw_f, gv);
+      t = __fsub_rn(t, db[j]);
+      t = __fsub_rn(t, __fmul_rn(xh, dg[j]));
+      o[j] = __fmul_rn(kk[j], t);
+    }
   };
   constexpr int U = 4;
   for (; rt.r - (U - 1) * rt.step >= rt.first; rt.r -= U * rt.step) {
@@ -538,27 +549,6 @@ int bn_training(cudaStream_t s, const float* x, const int64_t* x_shape, const fl
                           used_blocks);
 }
 
-// The reduction half of the backward: partials of (sum dy, sum dy * x_hat)
-// then the per-channel finalize (grad_beta, grad_gamma, k1, inv_std).
-int grad_reduce(cudaStream_t s, const float* grad_y, const float* x, int64_t rows, int64_t C, const float* gamma,
-                const float* beta, const float* saved_mean, const float* saved_var, float epsilon, bool relu,
-                bool vec_ok, float* grad_gamma, float* grad_beta, float* k1, float* inv, int* used_blocks_out) {
-  const DeviceInfo* d = nullptr;
-  B2_RETURN_IF_ERROR(device_info(&d));
-  const ChunkGeom geo = chunk_geom(C, vec_ok);
-  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
-  Scratch part;
-  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
-  int used_blocks = 0;
-  B2_RETURN_IF_ERROR(launch_partials(s, relu ? 2 : 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C,
-                                     vec_ok, d, part.as<float2>(), &used_blocks, gamma, beta));
-  bn_grad_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
-                                                               epsilon, gamma, saved_var, grad_beta, grad_gamma, k1,
-                                                               inv);
-  *used_blocks_out = used_blocks;
-  return check_launch(s, "bn_grad_finalize");
-}
-
 // Backward: dx, dgamma, dbeta from dy (relu: dy = (y > 0 ? dz : 0) with y
 // recomputed from x, the statistics, gamma and beta).
 int bn_grad(cudaStream_t s, const float* grad_y, const int64_t* grad_y_shape, const float* x,
@@ -574,18 +564,21 @@ int bn_grad(cudaStream_t s, const float* grad_y, const int64_t* grad_y_shape, co
   if (C == 0) return B2_OK;
   const DeviceInfo* d = nullptr;
   B2_RETURN_IF_ERROR(device_info(&d));
-  // the reduction's order depends on x and grad_y only (bn_grad_reduce takes
-  // the same path), the elementwise pass also needs grad_x aligned
-  const bool vec_red = (C % 4 == 0) && aligned16(x) && aligned16(grad_y);
-  const bool vec_ok = vec_red && aligned16(grad_x);
+  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(grad_y) && aligned16(grad_x);
   const ChunkGeom geo = chunk_geom(C, vec_ok);
-  Scratch chan;
+  const int blocks = row_blocks(rows, geo.chunks, d->sm_count);
+  Scratch part, chan;
+  B2_RETURN_IF_ERROR(part.alloc(sizeof(float2) * blocks * C, s));
   B2_RETURN_IF_ERROR(chan.alloc(sizeof(float) * 2 * C, s));
   float* k1 = chan.as<float>();
   float* inv = k1 + C;
   int used_blocks = 0;
-  B2_RETURN_IF_ERROR(grad_reduce(s, grad_y, x, rows, C, gamma, beta, saved_mean, saved_var, epsilon, relu,
-                                 vec_red, grad_gamma, grad_beta, k1, inv, &used_blocks));
+  B2_RETURN_IF_ERROR(launch_partials(s, relu ? 2 : 1, x, grad_y, saved_mean, saved_var, epsilon, rows, (int)C,
+                                     vec_ok, d, part.as<float2>(), &used_blocks, gamma, beta));
+  bn_grad_finalize_kernel<<<(unsigned)C, kFinThreads, 0, s>>>(part.as<float2>(), used_blocks, (int)C, rows,
+                                                               epsilon, gamma, saved_var, grad_beta, grad_gamma, k1,
+                                                               inv);
+  B2_RETURN_IF_ERROR(check_launch(s, "bn_grad_finalize"));
   if (total == 0) return B2_OK;
   const float nhw_f = (float)(int)rows;
   int rg = 0;
@@ -609,16 +602,6 @@ int bn_grad(cudaStream_t s, const float* grad_y, const int64_t* grad_y_shape, co
 }
 
 }  // namespace
-
-int bn_grad_reduce(cudaStream_t s, const float* grad_y, const float* x, int64_t rows, int64_t C,
-                   const float* gamma, const float* beta, const float* saved_mean, const float* saved_var,
-                   float epsilon, bool relu, float* grad_gamma, float* grad_beta, float* k1, float* inv_std) {
-  const bool vec_ok = (C % 4 == 0) && aligned16(x) && aligned16(grad_y);
-  int used = 0;
-  return grad_reduce(s, grad_y, x, rows, C, gamma, beta, saved_mean, saved_var, epsilon, relu, vec_ok, grad_gamma,
-                     grad_beta, k1, inv_std, &used);
-}
-
 }  // namespace b2
 
 using namespace b2;

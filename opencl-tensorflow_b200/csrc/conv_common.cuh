@@ -64,10 +64,4 @@ int conv_direct_forward(const ConvGeom& g, const float* x, const float* w, float
 int conv_direct_backprop_input(const ConvGeom& g, const float* dy, const float* w, float* dx, cudaStream_t s);
 int conv_direct_backprop_filter(const ConvGeom& g, const float* x, const float* dy, float* dw, cudaStream_t s);
 
-// Filter gradient of a 7-wide, 3-input-channel, column-stride-2 Conv2D (the
-// README stem) on the CUDA cores (conv_wgrad.cu); ybn (the fused BatchNorm
-// input) may be null.
-bool conv_wgrad_rows_ok(const ConvGeom& g, const float* x, const float* dy, const float* ybn);
-int conv_wgrad_rows(const ConvGeom& g, const float* x, const float* dy, float* dw, cudaStream_t s);
-
 }  // namespace b2

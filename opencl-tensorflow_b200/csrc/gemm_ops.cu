@@ -29,7 +29,6 @@
 
 namespace b2 {
 unsigned int dw_timeouts();  // depthwise.cu
-unsigned int wg_timeouts();  // conv_wgrad.cu
 
 namespace tc {
 
@@ -756,7 +755,6 @@ int b2_conv2d_backprop_filter(b2_stream_t stream, const float* input, const int6
   const int64_t M = g.kH * g.kW * g.Ci, K = g.N * g.Ho * g.Wo;
   if (M == 0 || g.Co == 0) return B2_OK;
   if (conv_direct_ok(g)) return conv_direct_backprop_filter(g, input, out_backprop, output, s);
-  if (conv_wgrad_rows_ok(g, input, out_backprop, nullptr)) return conv_wgrad_rows(g, input, out_backprop, output, s);
   const MNMajor bv{out_backprop, g.Co, g.Co};
   if (is_pointwise(g)) {
     const MNMajor av{input, g.Ci, g.Ci};
@@ -852,7 +850,7 @@ int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_
 int b2_device_timeouts(unsigned int* count) {
   clear_error();
   B2_CUDA_OR_RETURN(cudaMemcpyFromSymbol(count, g_tc_timeouts, sizeof(unsigned int)));
-  *count += b2::dw_timeouts() + b2::wg_timeouts();
+  *count += b2::dw_timeouts();
   return B2_OK;
 }
 

@@ -73,8 +73,6 @@ _SIGS = {
     "b2_batch_norm_update_moving": [_P, _P, _P, _P, _P, _I64, _F32, _F32],
     "b2_batch_norm_relu_training": [_P, _P, _P, _P, _I64, _P, _I64, _F32, _P, _P, _P, _P, _P, _F32, _F32],
     "b2_batch_norm_relu_grad": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _P, _P],
-    "b2_conv2d_batch_norm_relu_backprop_filter": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P, _I, _S, _P,
-                                                  _P, _P],
     "b2_dense": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_relu": [_P, _P, _P, _P, _P, _P, _I64, _P],
     "b2_dense_backprop_input": [_P, _P, _P, _P, _P, _P],
@@ -365,41 +363,6 @@ def _k_batch_norm_relu_training(x, gamma, beta, epsilon=1e-3, moving=None):
                                                 _p(mv) if mv is not None else None, float(mom),
                                                 float(1.0 - mom)))
     return z, mean, var
-
-
-def _k_conv2d_batch_norm_relu_training(input, filter, gamma, beta, strides, padding, epsilon=1e-3, moving=None):
-    """OpenclConv2d then the fused BatchNorm -> ReLU; returns (z, y, mean,
-    var) with y the convolution's output (the BatchNorm input)."""
-    y = _k_conv2d(input, filter, strides, padding)
-    z, mean, var = _k_batch_norm_relu_training(y, gamma, beta, epsilon, moving)
-    return z, y, mean, var
-
-
-def _k_conv2d_batch_norm_relu_backprop_filter(input, filter_sizes, grad_z, bn_input, gamma, beta, saved_mean,
-                                              saved_var, strides, padding, epsilon=1e-3):
-    x = _input(input, "input")
-    sizes = _host_ints(filter_sizes, 4, "filter_sizes")
-    dz = _input(grad_z, "grad_z")
-    y = _input(bn_input, "bn_input")
-    g, b = _input(gamma, "gamma"), _input(beta, "beta")
-    m, v = _input(saved_mean, "saved_mean"), _input(saved_var, "saved_var")
-    _rank(x, 4, "input must be rank 4")
-    _rank(dz, 4, "grad_z must be rank 4")
-    if tuple(y.shape) != tuple(dz.shape):
-        raise errors.InvalidArgumentError("grad_z and bn_input must have the same shape")
-    C = dz.shape[3]
-    for t, name in ((g, "gamma"), (b, "beta"), (m, "saved_mean"), (v, "saved_var")):
-        if t.numel() != C:
-            raise errors.InvalidArgumentError(f"{name} must have {C} elements")
-    st, ns = _strides_arr(strides)
-    dw = torch.empty(tuple(sizes), device=x.device, dtype=torch.float32)
-    gg = torch.empty(C, device=x.device, dtype=torch.float32)
-    gb = torch.empty(C, device=x.device, dtype=torch.float32)
-    with _on_device(x):
-        _check(_lib.b2_conv2d_batch_norm_relu_backprop_filter(
-            _stream(x), _p(x), _I64x4(*x.shape), _I32x4(*sizes), _p(dz), _p(y), _I64x4(*dz.shape), _p(g), _p(b),
-            _p(m), _p(v), float(epsilon), st, ns, _padding(padding), _p(dw), _p(gg), _p(gb)))
-    return dw, gg, gb
 
 
 def _k_batch_norm_relu_grad(grad_z, x, gamma, beta, saved_mean, saved_var, epsilon=1e-3):
@@ -789,35 +752,14 @@ def _mk_fused_ops():
         """relu(x @ W + b) with the ReLU in the GEMM's epilogue."""
         return _apply("OpenclDenseRelu", _k_dense_relu, (x, w, b), {})
 
-    def opencl_conv2d_batch_norm_relu_training(input, filter, gamma, beta, strides, padding, epsilon=1e-3,
-                                               moving=None):
-        """relu(BN(conv2d(input, filter))) -> (z, y, mean, var), y the conv
-        output.  Its gradient, when the input needs none (a network's first
-        layer), never materialises the BatchNorm input gradient."""
-        attrs = {"strides": list(strides), "padding": padding, "epsilon": float(epsilon)}
-        if moving is not None:
-            attrs["moving"] = moving
-        return _apply("OpenclConv2dBatchNormReluTraining", _k_conv2d_batch_norm_relu_training,
-                      (input, filter, gamma, beta), attrs, nondiff=(1, 2, 3))
-
-    def opencl_conv2d_batch_norm_relu_backprop_filter(input, filter_sizes, grad_z, bn_input, gamma, beta, saved_mean,
-                                                      saved_var, strides, padding, epsilon=1e-3):
-        """(grad_filter, grad_gamma, grad_beta) of the op above, bit for bit
-        the ReLU -> BatchNorm -> filter gradients in sequence."""
-        return _k_conv2d_batch_norm_relu_backprop_filter(input, filter_sizes, grad_z, bn_input, gamma, beta,
-                                                         saved_mean, saved_var, list(strides), padding,
-                                                         float(epsilon))
-
-    for k in ("opencl_batch_norm_relu_training", "opencl_batch_norm_relu_grad", "opencl_dense_relu",
-              "opencl_conv2d_batch_norm_relu_training", "opencl_conv2d_batch_norm_relu_backprop_filter"):
+    for k in ("opencl_batch_norm_relu_training", "opencl_batch_norm_relu_grad", "opencl_dense_relu"):
         setattr(ns, k, _traced(k, locals()[k]))
     return ns
 
 
 fused_ops = _mk_fused_ops()
-"""Ops with no counterpart in the reference: sequences its layers run back to
-back (BatchNormTraining -> Relu, Dense -> Relu, Conv2D -> BatchNormTraining
--> Relu), fused, with bit-identical results."""
+"""Ops with no counterpart in the reference: pairs its layers run back to back
+(BatchNormTraining -> Relu, Dense -> Relu), fused, with bit-identical results."""
 
 
 def _mk_step_ops():

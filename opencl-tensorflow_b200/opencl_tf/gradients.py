@@ -76,27 +76,6 @@ def _batch_norm_relu_training_grad(op, grad_z, grad_mean=None, grad_var=None):
     return [gx, ggamma, gbeta]
 
 
-@RegisterGradient("OpenclConv2dBatchNormReluTraining")
-def _conv2d_batch_norm_relu_training_grad(op, grad_z, grad_y=None, grad_mean=None, grad_var=None):
-    """The gradients of Conv2D -> BatchNorm -> ReLU: BatchNorm->ReLU's, then
-    the two Conv2D gradients.  Without an input gradient (the network's first
-    layer) the filter gradient takes the BatchNorm input gradient straight from
-    grad_z and y (fused_ops), with the same bits."""
-    x, w, gamma, beta = op.inputs
-    _z, y, saved_mean, saved_var = op.outputs
-    strides, padding, eps = op.get_attr("strides"), op.get_attr("padding"), op.get_attr("epsilon")
-    need_x = op.needs_input_grad[0]
-    if not need_x:
-        dw, ggamma, gbeta = fused_ops.opencl_conv2d_batch_norm_relu_backprop_filter(
-            x, _host_shape(w), grad_z, y, gamma, beta, saved_mean, saved_var, strides, padding, epsilon=eps)
-        return [None, dw, ggamma, gbeta]
-    gy, ggamma, gbeta = fused_ops.opencl_batch_norm_relu_grad(grad_z, y, gamma, beta, saved_mean, saved_var,
-                                                            epsilon=eps)
-    dx = raw_ops.opencl_conv2d_backprop_input(_host_shape(x), w, gy, strides=strides, padding=padding)
-    dw = raw_ops.opencl_conv2d_backprop_filter(x, _host_shape(w), gy, strides=strides, padding=padding)
-    return [dx, dw, ggamma, gbeta]
-
-
 @RegisterGradient("OpenclSigmoid")
 def _sigmoid_grad(op, grad):
     return [raw_ops.opencl_sigmoid_grad(op.outputs[0], grad)]

@@ -35,7 +35,6 @@ from typing import Sequence
 import torch
 from torch import nn
 
-from ._library import fused_ops
 from .layers import (OpenCLBatchNormalization, OpenCLConv2D, OpenCLDense, OpenCLDepthwiseConv2D, OpenCLReLU,
                      OpenCLSigmoid, OpenCLUpSampling2D)
 
@@ -116,22 +115,8 @@ class BuildModel(nn.Module):
             return bn.forward_relu(x, training=training)
         return relu(bn(x, training=training))
 
-    def _stem(self, x, training):
-        """conv -> BN -> ReLU; fused into one op when training (the gradient
-        then skips the stem's BatchNorm input gradient, which only the filter
-        gradient reads: the image batch needs no gradient)."""
-        if training is None:
-            training = self.training
-        if self.fuse_bn_relu and bool(training):
-            conv, bn = self.stem_conv, self.stem_bn
-            z, _y, _mean, _var = fused_ops.opencl_conv2d_batch_norm_relu_training(
-                x, conv.kernel, bn.gamma, bn.beta, (1, conv.strides[0], conv.strides[1], 1), conv.padding,
-                epsilon=bn.epsilon, moving=(bn.moving_mean, bn.moving_var, bn.momentum))
-            return z
-        return self._bn_relu(self.stem_bn, self.stem_relu, self.stem_conv(x), training)
-
     def forward(self, x, training=None):
-        x = self._stem(x, training)
+        x = self._bn_relu(self.stem_bn, self.stem_relu, self.stem_conv(x), training)
         for dw, bn1, r1, pw, bn2, r2 in self.blocks:
             x = self._bn_relu(bn1, r1, dw(x), training)
             x = self._bn_relu(bn2, r2, pw(x), training)

@@ -29,8 +29,7 @@ _KERNELS = ["_k_conv2d", "_k_conv2d_backprop_input", "_k_conv2d_backprop_filter"
             "_k_sigmoid", "_k_sigmoid_grad", "_k_batch_norm_training", "_k_batch_norm_inference",
             "_k_batch_norm_grad", "_k_dense", "_k_dense_relu", "_k_dense_backprop_input", "_k_dense_backprop_weight",
             "_k_dense_backprop_bias", "_k_upsampling_bilinear2d", "_k_upsampling_bilinear2d_grad",
-            "_k_batch_norm_relu_training", "_k_batch_norm_relu_grad", "_k_mse_loss", "_k_mse_loss_grad",
-            "_k_conv2d_batch_norm_relu_training", "_k_conv2d_batch_norm_relu_backprop_filter"]
+            "_k_batch_norm_relu_training", "_k_batch_norm_relu_grad", "_k_mse_loss", "_k_mse_loss_grad"]
 
 
 def peaks(path=None) -> dict:
@@ -94,12 +93,6 @@ def work(name, args, kw, out) -> tuple[float, float]:
         else:
             dy, dw = args[2], outs[0]
             flops = 2.0 * dy.numel() * dw.shape[0] * dw.shape[1] * dw.shape[2]
-    elif name == "conv2d_batch_norm_relu_training":
-        y, w = outs[1], args[1]
-        flops = 2.0 * y.numel() * w.shape[0] * w.shape[1] * w.shape[2]
-    elif name == "conv2d_batch_norm_relu_backprop_filter":
-        dz, dw = args[2], outs[0]
-        flops = 2.0 * dz.numel() * dw.shape[0] * dw.shape[1] * dw.shape[2]
     elif name.startswith("depthwise"):
         w = args[1] if name != "depthwise_conv2d_backprop_filter" else outs[0]
         taps = w.shape[0] * w.shape[1]

@@ -37,10 +37,8 @@ def test_gradient_registry_matches_reference_wiring():
     reference = {"OpenclConv2d", "OpenclDepthwiseConv2d", "OpenclRelu", "OpenclBatchNormTraining", "OpenclSigmoid",
                  "OpenclDense", "OpenclUpsamplingBilinear2d"}
     # the reference's registrations, plus the extensions (not reference ops): the fused
-    # BatchNorm -> ReLU, Dense -> ReLU and Conv2D -> BatchNorm -> ReLU sequences and the
-    # training step's MSE loss
-    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining", "OpenclDenseRelu", "OpenclMseLoss",
-                                           "OpenclConv2dBatchNormReluTraining"}
+    # BatchNorm -> ReLU pair and the training step's MSE loss
+    assert set(_GRADIENTS) == reference | {"OpenclBatchNormReluTraining", "OpenclDenseRelu", "OpenclMseLoss"}
     assert "OpenclBatchNormInference" not in _GRADIENTS
 
 
