@@ -37,14 +37,13 @@
 //                (tcgen05.mma kind::tf32, A from TMEM, B from shared memory),
 //                commits OP_EMPTY per operand stage and CHUNK_FULL per chunk
 //                (at most kChunkKB k-blocks).
-//   warps 2-17   converters, two groups of eight warps (two per TMEM lane
-//                quarter, each taking 16 of the 32 columns) on alternate
-//                k-blocks: wait RAW_FULL, read their half row of A and a
-//                share of B, release the raw stage, wait for a free operand
-//                stage, write A into its TMEM slot (tcgen05.st) and B hi / lo
-//                into its shared-memory tiles, fence both proxies, arrive
-//                OP_FULL.
-//   warps 18-21  epilogue: per chunk fold P into S with round-to-nearest fp32
+//   warps 2-9    converters, two groups of four warps (one per TMEM lane
+//                quarter) on alternate k-blocks: wait RAW_FULL, read their
+//                row of A and a share of B, release the raw stage, wait for a
+//                free operand stage, write A into its TMEM slot (tcgen05.st)
+//                and B hi / lo into its shared-memory tiles, fence both
+//                proxies, arrive OP_FULL.
+//   warps 10-13  epilogue: per chunk fold P into S with round-to-nearest fp32
 //                adds; after the tile's last chunk, add the bias, write the
 //                warp's 32 x BN block as 128-byte-swizzled 32 x 32 pieces into
 //                its shared buffer and store them with TMA (clipped to D), so
@@ -72,10 +71,8 @@ namespace tc {
 constexpr int kTmaWarp = 0;
 constexpr int kTmaMmaWarp = 1;
 constexpr int kConvWarp0 = 2;
-constexpr int kGroupWarps = 8;                     // warps of one converter group: two per TMEM lane quarter
-constexpr int kKParts = kGroupWarps / 4;            // each converts BK / kKParts of the k-block's columns
-constexpr int kConvWarps = 2 * kGroupWarps;         // two groups on alternate k-blocks
-constexpr int kTmaEpiWarp0 = kConvWarp0 + kConvWarps;  // 18 .. 21: lane quarters 2, 3, 0, 1
+constexpr int kConvWarps = 8;
+constexpr int kTmaEpiWarp0 = kConvWarp0 + kConvWarps;  // 10 .. 13: lane quarters 2, 3, 0, 1
 constexpr int kTmaThreads = 32 * (kTmaEpiWarp0 + 4);
 constexpr int kTmaMaxStages = 8;    // raw (TMA) stages
 constexpr int kTmaMaxOpStages = 4;  // operand stages (B hi/lo in smem + A hi/lo in TMEM)
@@ -239,16 +236,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 16 consecutive TMEM columns of this warp's 32 lanes; pair with tmem_wait_ld.
-__device__ __forceinline__ void tmem_ld16u(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
 
 // 3xTF32 operand split: x = hi + lo with hi = tf32(x) rounded to nearest,
 // ties away from zero (one `cvt.rna.tf32.f32`, the same bits as adding half a
@@ -448,16 +435,16 @@ __device__ __forceinline__ RowGather row_gather(const TmaProblem& p, const TmaTi
   return g;
 }
 
-// The 16-element half h (k0 + 16h .. +15) of this thread's A row for the
-// k-block at k0.
+// Both 16-element halves of this thread's A row for the k-block at k0.
 template <int AK>
 __device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem& p, const RowGather& g, int k0,
-                                            const int* imtab, int h, float (&v)[16]) {
+                                            const int* imtab, float (&v)[2][16]) {
   const ConvRows& cr = p.cr;
   const float* xs = reinterpret_cast<const float*>(raw) + g.base;  // [span][wcp], column c at c + xpad
   if constexpr (AK == kAFpropRows) {
     const int K = (int)p.K;  // < 2^31 on this path (checked on the host)
-    {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
       const int k = k0 + 16 * h;
       const int4* t4 = reinterpret_cast<const int4*>(imtab + k);  // padded table: always in bounds
       int off[16];
@@ -471,10 +458,10 @@ __device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem
       }
       if (k + 16 <= K) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = xs[off[i]];
+        for (int i = 0; i < 16; ++i) v[h][i] = xs[off[i]];
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = k + i < K ? xs[off[i]] : 0.0f;
+        for (int i = 0; i < 16; ++i) v[h][i] = k + i < K ? xs[off[i]] : 0.0f;
       }
     }
   } else {
@@ -483,7 +470,8 @@ __device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem
     const int ro0 = (int)p.wo_div.div((uint32_t)k0);
     const int wo0 = k0 - ro0 * cr.Wo;
     const int step = cr.sW * cr.Ci, wrap = cr.sH * cr.wcp - (cr.Wo - 1) * step;
-    {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
       int wo = wo0 + 16 * h, b = 0;
       while (wo >= cr.Wo) {  // at most 16 / Wo + 1 times
         wo -= cr.Wo;
@@ -494,17 +482,17 @@ __device__ __forceinline__ void read_a_rows(const uint8_t* raw, const TmaProblem
       const float* xb = xs + b;
       if (n1 >= 16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = xb[i * step];
+        for (int i = 0; i < 16; ++i) v[h][i] = xb[i * step];
       } else if (cr.Wo >= 16) {
         // one row change: every offset is independent of the previous one
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = xb[i * step + (i >= n1 ? wrap - step : 0)];
+        for (int i = 0; i < 16; ++i) v[h][i] = xb[i * step + (i >= n1 ? wrap - step : 0)];
       } else {
         int c = 0;
         wo = cr.Wo - n1;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          v[i] = xb[c];
+          v[h][i] = xb[c];
           if (++wo == cr.Wo) {
             wo = 0;
             c += wrap;
@@ -525,7 +513,7 @@ __device__ __forceinline__ void split16(const float (&v)[16], uint32_t (&hv)[16]
   }
 }
 
-constexpr int kGroupThreads = 32 * kGroupWarps;  // one converter group
+constexpr int kGroupThreads = 128;  // one converter group: a warp per TMEM lane quarter
 constexpr int kMaxBWords = kTmaMaxBN * BK * 4 / 16 / kGroupThreads;  // 16-byte B words per thread
 
 template <int AK, bool kBK>
@@ -571,10 +559,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     wait_state_init(ws, p.wait);
     for (int s = 0; s < raw_stages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kGroupWarps);
+      mbar_init(&raw_empty[s], 4);
     }
     for (int s = 0; s < op_stages; ++s) {
-      mbar_init(&op_full[s], kGroupWarps);
+      mbar_init(&op_full[s], 4);
       mbar_init(&op_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -651,17 +639,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
   } else if (warp >= kConvWarp0 && warp < kTmaEpiWarp0) {
     // ---------------------------------------------------------- converters
-    // Two groups of kGroupWarps warps take alternate k-blocks; in a group,
-    // the warps of lane quarter q (warp % 4, the TMEM lanes a warp may
-    // access) convert rows 32q .. 32q+31 of A (one row a thread), each its
-    // own kKParts-th of the k-block's columns, and every thread a share of
-    // B's 16-byte words.  Splitting the columns shortens each warp's
-    // dependent chain of loads, splits and TMEM stores per k-block.
-    const int cw = warp - kConvWarp0;
-    const int group = cw / kGroupWarps;
+    // Two groups of four warps take alternate k-blocks; in a group, the warp
+    // of lane quarter q converts rows 32q .. 32q+31 of A (one row a thread)
+    // and a share of B's 16-byte words.
+    const int group = (warp - kConvWarp0) >> 2;
     const int quarter = warp & 3;
-    const int part = (cw % kGroupWarps) >> 2;  // which kKParts-th of the columns
-    const int gt = (cw % kGroupWarps) * 32 + lane;
+    const int gt = ((warp - kConvWarp0) & 3) * 32 + lane;
     const int row = quarter * 32 + lane;
     const uint32_t a_taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + a_col0;
     const int b_words = bn * BK * 4 / 16;
@@ -708,14 +691,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           break;
         }
         const uint8_t* raw = smem + (size_t)sr * plan.raw_bytes;
-        constexpr int kHalves = 2 / kKParts;  // 16-column halves this warp converts
-        float va[kHalves][16];
+        float va[2][16];
         const int k0 = (int)(tc.k_begin + (int64_t)kb * BK);
-#pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh) {
-          const int h = part * kHalves + hh;
-          if constexpr (AK == kAFpropRows || AK == kAWgradRows) read_a_rows<AK>(raw, p, rg, k0, imtab, h, va[hh]);
-          else read_a_row<AK>(raw, row, h, va[hh]);
+        if constexpr (AK == kAFpropRows || AK == kAWgradRows) {
+          read_a_rows<AK>(raw, p, rg, k0, imtab, va);
+        } else {
+          read_a_row<AK>(raw, row, 0, va[0]);
+          read_a_row<AK>(raw, row, 1, va[1]);
         }
         uint4 wb[kMaxBWords];
 #pragma unroll
@@ -731,10 +713,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t slot = a_taddr + sq * kASlotCols;
 #pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh) {
-          const uint32_t h = (uint32_t)(part * kHalves + hh);
+        for (int h = 0; h < 2; ++h) {
           uint32_t hv[16], lv[16];
-          split16(va[hh], hv, lv);
+          split16(va[h], hv, lv);
           tmem_st16u(slot + 16u * h, hv);
           tmem_st16u(slot + BK + 16u * h, lv);
         }
@@ -830,48 +811,45 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           pending = false;
         }
         const uint32_t p_addr = tmem_base + lane_off + (uint32_t)a * acc_cols;
-        // 16 columns at a time (the converter warps leave few registers)
-        for (int c = 0; c < bn; c += 16) {
-          float v[16];
+        for (int c = 0; c < bn; c += 32) {
+          float v[32];
           if (nch > 0) {
-            uint32_t pv[16];
-            tmem_ld16u(p_addr + (uint32_t)c, pv);
+            uint32_t pv[32];
+            tmem_ld32(p_addr + (uint32_t)c, pv);
             if (!first) {
-              uint32_t sv[16];
-              tmem_ld16u(s_addr + (uint32_t)c, sv);
+              uint32_t sv[32];
+              tmem_ld32(s_addr + (uint32_t)c, sv);
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = __fadd_rn(__uint_as_float(sv[e]), __uint_as_float(pv[e]));
+              for (int e = 0; e < 32; ++e) v[e] = __fadd_rn(__uint_as_float(sv[e]), __uint_as_float(pv[e]));
             } else {
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(pv[e]);
+              for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(pv[e]);
             }
           } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+            for (int e = 0; e < 32; ++e) v[e] = 0.0f;
           }
           if (!last) {
-            tmem_st16(s_addr + (uint32_t)c, v);
+            tmem_st16(s_addr + (uint32_t)c, *reinterpret_cast<const float(*)[16]>(v));
+            tmem_st16(s_addr + (uint32_t)c + 16u, *reinterpret_cast<const float(*)[16]>(v + 16));
             continue;
           }
           if (p.bias) {
             const int64_t n = tc.n0 + c;
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
+            for (int e = 0; e < 32; ++e)
               if (n + e < p.N) v[e] += __ldg(p.bias + n + e);
           }
           if (p.relu) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = v[e] > 0.0f ? v[e] : 0.0f;  // fmax(v, 0): NaN -> 0, -0 -> +0
+            for (int e = 0; e < 32; ++e) v[e] = v[e] > 0.0f ? v[e] : 0.0f;  // fmax(v, 0): NaN -> 0, -0 -> +0
           }
-          // 32 x 32 block, 128-byte swizzled rows; these 16 columns are 16-byte
-          // chunks jc .. jc + 3 of the row
-          uint8_t* buf = ebuf + (c / 32) * kEpiBuf;
-          const int jc = (c & 31) / 4;
+          uint8_t* buf = ebuf + (c / 32) * kEpiBuf;  // 32 x 32 block, 128-byte swizzled rows
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<float4*>(buf + lane * 128 + (((jc + j) ^ (lane & 7)) << 4)) =
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
         if (nch > 0) {
