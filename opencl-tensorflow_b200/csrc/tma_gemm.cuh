@@ -754,25 +754,39 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
           const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
-          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          for (int kb = kb0; kb < kb1 && ok;) {
+            // The wait and the thread-sync fence stall this thread for about
+            // as long as four MMAs take, so when the next operand stage is
+            // ready too (converters usually run ahead), both k-blocks are
+            // issued behind one fence.  The stage after sq is tested without
+            // blocking; its previous phase is one this thread consumed, so a
+            // completed parity can only mean the current use.
             if (!mbar_wait(&op_full[sq], lap_q & 1u, ws)) {
               ok = false;
               break;
             }
+            const uint32_t sq1 = sq + 1 == Q ? 0u : sq + 1, lap1 = sq + 1 == Q ? lap_q + 1 : lap_q;
+            const int nkb = (kb + 1 < kb1 && mbar_try_wait(&op_full[sq1], lap1 & 1u)) ? 2 : 1;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = tmem_base + a_col0 + sq * kASlotCols, a_lo = a_hi + BK;
-            const uint32_t b_hi = smem_u32(smem + plan.op_offset + (size_t)(bres ? (uint32_t)kb : sq) * plan.op_bytes);
-            const uint32_t b_lo = b_hi + plan.b_bytes;
+            for (int u = 0; u < nkb; ++u, ++kb, ++it) {
+              const uint32_t a_hi = tmem_base + a_col0 + sq * kASlotCols, a_lo = a_hi + BK;
+              const uint32_t b_hi =
+                  smem_u32(smem + plan.op_offset + (size_t)(bres ? (uint32_t)kb : sq) * plan.op_bytes);
+              // descriptors of the 8-wide k steps differ only in the start
+              // address field: +32 B (K-major) or +1024 B (MN-major) a step
+              const uint64_t dh = operand_desc<kBK>(b_hi, 0), dl = operand_desc<kBK>(b_hi + plan.b_bytes, 0);
+              constexpr uint64_t kStep = kBK ? 2u : 64u;  // in the descriptor's 16-byte units
 #pragma unroll
-            for (int j = 0; j < BK / 8; ++j) {
-              mma_tf32_ts(d, a_lo + 8u * j, operand_desc<kBK>(b_hi, j), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-              mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_lo, j), idesc, 1u);
-              mma_tf32_ts(d, a_hi + 8u * j, operand_desc<kBK>(b_hi, j), idesc, 1u);
-            }
-            mma_commit(&op_empty[sq]);
-            if (++sq == Q) {
-              sq = 0;
-              ++lap_q;
+              for (int j = 0; j < BK / 8; ++j) {
+                mma_tf32_ts(d, a_lo + 8u * j, dh + kStep * j, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+                mma_tf32_ts(d, a_hi + 8u * j, dl + kStep * j, idesc, 1u);
+                mma_tf32_ts(d, a_hi + 8u * j, dh + kStep * j, idesc, 1u);
+              }
+              mma_commit(&op_empty[sq]);
+              if (++sq == Q) {
+                sq = 0;
+                ++lap_q;
+              }
             }
           }
           mma_commit(&chunk_full[a]);
