@@ -104,6 +104,14 @@ int b2_pool_trim(void);
 /* Kernels this library has enqueued since it was loaded (all devices). */
 int b2_kernel_launch_count(uint64_t* count);
 
+/* Leave `count` SMs of every device free of this library's persistent
+ * (one-CTA-per-SM) tensor-core kernels, for kernels that must run beside
+ * them -- NCCL's all-reduce during data-parallel training, which otherwise
+ * waits for SMs until the GEMM in flight ends.  0 (the default) uses every
+ * SM.  Only how many CTAs share the same tiles changes, not the results.
+ * Applies to launches after the call (a captured graph keeps its grids). */
+int b2_set_reserved_sms(int count);
+
 /* ------------------------------------------------------------- Conv2D */
 
 /* OpenclConv2d(input, filter; strides, padding) -> output

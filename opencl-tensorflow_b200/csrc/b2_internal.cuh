@@ -92,6 +92,12 @@ struct DeviceInfo {
 // first use; fails with B2_ERR_NO_DEVICE for anything but an sm_100 part).
 int device_info(const DeviceInfo** out);
 
+// CTAs of a persistent (one CTA per SM) kernel: the SM count less the SMs
+// b2_set_reserved_sms keeps free for kernels that run beside this library's
+// (NCCL's, during data-parallel training), at least 1.  Only the number of
+// CTAs that loop over the same tiles changes, so results do not.
+int persistent_ctas(const DeviceInfo* d);
+
 // ---------------------------------------------------------------- scratch
 
 // Stream-ordered scratch from the device's caching pool.  Legal inside CUDA

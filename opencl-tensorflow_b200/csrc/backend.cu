@@ -163,6 +163,13 @@ int check_launch(cudaStream_t s, const char* what) {
   return B2_OK;
 }
 
+std::atomic<int> g_reserved_sms{0};
+
+int persistent_ctas(const DeviceInfo* d) {
+  const int n = d->sm_count - g_reserved_sms.load(std::memory_order_relaxed);
+  return n > 0 ? n : 1;
+}
+
 WaitParams wait_params() {
   return WaitParams{g_wait_limit_ns.load(std::memory_order_relaxed), g_expired_dev};
 }
@@ -287,6 +294,13 @@ int b2_pool_stats(b2_pool_stats_t* out) {
 
 int b2_kernel_launch_count(uint64_t* count) {
   *count = g_launches.load(std::memory_order_relaxed);
+  return B2_OK;
+}
+
+int b2_set_reserved_sms(int count) {
+  clear_error();
+  B2_REQUIRE(count >= 0, "the reserved SM count must be non-negative");
+  g_reserved_sms.store(count, std::memory_order_relaxed);
   return B2_OK;
 }
 

@@ -471,7 +471,8 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   // then loaded and split once per CTA instead of once per k-block.
   const int64_t nt = ceil_div(N, bn);
   int b_res_kb = 0;
-  int grid = (int)(tiles * splits < d->sm_count ? tiles * splits : d->sm_count);
+  const int ctas = persistent_ctas(d);
+  int grid = (int)(tiles * splits < ctas ? tiles * splits : ctas);
   if (splits == 1 && K <= (int64_t)kTmaMaxResKB * BK && grid / nt * nt > 0 &&
       ceil_div(K, BK) * 2 * (int64_t)bn * BK * 4 <= kTmaMaxResBytes) {
     tma_stages(bn, use_s, table, d->max_smem_optin, &raw_stages, &op_stages, (int)ceil_div(K, BK));

@@ -606,7 +606,8 @@ int launch_gemm(P prob, int bn, cudaStream_t s, const char* name) {
   B2_RETURN_IF_ERROR(opt_in.ensure(reinterpret_cast<const void*>(tc_gemm_kernel<P>), d->device, (int)plan.total));
   prob.wait = wait_params();
   const int64_t tiles = ceil_div(prob.N, bn) * ceil_div(prob.M, BM) * prob.splits;
-  const int grid = (int)(tiles < d->sm_count ? tiles : d->sm_count);
+  const int ctas = persistent_ctas(d);
+  const int grid = (int)(tiles < ctas ? tiles : ctas);
   tc_gemm_kernel<P><<<grid, kThreads, plan.total, s>>>(prob, bn, stages);
   return check_launch(s, name);
 }

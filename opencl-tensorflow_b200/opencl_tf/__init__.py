@@ -24,7 +24,7 @@ training step from one CUDA graph.
 """
 
 from ._library import (raw_ops, fused_ops, step_ops, init, pool_stats, pool_trim, device_timeouts, stream_status,
-                       set_wait_limit_ns, library_path)
+                       set_wait_limit_ns, set_reserved_sms, library_path)
 from .ops import (
     conv2d,
     conv2d_backprop_input,
@@ -62,7 +62,7 @@ __all__ = [
     "upsampling_bilinear_2d", "upsampling_bilinear_2d_grad",
     "fused_ops", "step_ops", "optimizers",
     "layers", "errors", "init", "pool_stats", "pool_trim", "device_timeouts", "stream_status",
-    "set_wait_limit_ns", "library_path",
+    "set_wait_limit_ns", "set_reserved_sms", "library_path",
 ]
 
 __version__ = "0.3.0+b200"

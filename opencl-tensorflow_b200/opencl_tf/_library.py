@@ -88,6 +88,7 @@ _SIGS = {
     "b2_device_timeouts": [ctypes.POINTER(ctypes.c_uint)],
     "b2_stream_status": [_P],
     "b2_set_wait_limit_ns": [ctypes.c_uint64],
+    "b2_set_reserved_sms": [_I],
     "b2_kernel_launch_count": [ctypes.POINTER(ctypes.c_uint64)],
 }
 for _name, _args in _SIGS.items():
@@ -821,6 +822,12 @@ def stream_status(device=None) -> None:
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
         _check(_lib.b2_stream_status(torch.cuda.current_stream(dev).cuda_stream))
+
+
+def set_reserved_sms(count: int) -> None:
+    """Keep ``count`` SMs free of the library's persistent tensor-core kernels
+    (for NCCL's kernels during data-parallel training); 0 uses every SM."""
+    _check(_lib.b2_set_reserved_sms(int(count)))
 
 
 def set_wait_limit_ns(limit_ns: int) -> None:

@@ -17,11 +17,13 @@ averages stay per replica, as on one device in the reference.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 from torch.distributed import distributed_c10d as c10d
 
-from ._library import step_ops
+from ._library import set_reserved_sms, step_ops
 from .optimizers import Adam
 
 
@@ -129,15 +131,24 @@ class GradientAverager:
 
 
 class TrainStep:
-    """fwd + MSE + bwd + gradient averaging + Adam for ``model`` on (x, y)."""
+    """fwd + MSE + bwd + gradient averaging + Adam for ``model`` on (x, y).
+
+    ``reserved_sms``: with more than one rank, SMs kept free of the library's
+    persistent tensor-core kernels so that NCCL's all-reduce kernels run
+    beside the backward pass instead of waiting for SMs (default: the
+    ``B2_RESERVED_SMS`` environment variable, else 0)."""
 
     def __init__(self, model: torch.nn.Module, lr: float = 1e-3, graphed: bool = True, warmup: int = 3,
-                 group=None):
+                 group=None, reserved_sms: int | None = None):
         self.model = model
         self.params = [p for p in model.parameters() if p.requires_grad]
         dev = self.params[0].device
         self.opt = Adam(self.params, learning_rate=lr)
         self.avg = GradientAverager(self.params, group)
+        if self.avg.world > 1 and dev.type == "cuda":
+            if reserved_sms is None:
+                reserved_sms = int(os.environ.get("B2_RESERVED_SMS", "0"))
+            set_reserved_sms(reserved_sms)
         self.graphed = graphed and dev.type == "cuda"
         self.warmup = warmup
         self.graph = None
