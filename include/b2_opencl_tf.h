@@ -108,8 +108,9 @@ int b2_kernel_launch_count(uint64_t* count);
  * (one-CTA-per-SM) tensor-core kernels, for kernels that must run beside
  * them -- NCCL's all-reduce during data-parallel training, which otherwise
  * waits for SMs until the GEMM in flight ends.  0 (the default) uses every
- * SM.  Only how many CTAs share the same tiles changes, not the results.
- * Applies to launches after the call (a captured graph keeps its grids). */
+ * SM.  Split-K GEMMs size their splits to the remaining SMs, so their sums
+ * are added in a different (still fixed) order than with 0.  Applies to
+ * launches after the call (a captured graph keeps its grids). */
 int b2_set_reserved_sms(int count);
 
 /* ------------------------------------------------------------- Conv2D */

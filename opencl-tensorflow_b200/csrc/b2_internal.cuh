@@ -94,8 +94,10 @@ int device_info(const DeviceInfo** out);
 
 // CTAs of a persistent (one CTA per SM) kernel: the SM count less the SMs
 // b2_set_reserved_sms keeps free for kernels that run beside this library's
-// (NCCL's, during data-parallel training), at least 1.  Only the number of
-// CTAs that loop over the same tiles changes, so results do not.
+// (NCCL's, during data-parallel training), at least 1.  Split-K GEMMs also
+// size their splits to it (so no CTA takes a second slice), which changes
+// the order of their additions: results stay deterministic for a given
+// setting, and every rank of a data-parallel job uses the same one.
 int persistent_ctas(const DeviceInfo* d);
 
 // ---------------------------------------------------------------- scratch

@@ -459,7 +459,7 @@ int run_tma_gemm(const ASpec& a, const MatOperand& b, int64_t M, int64_t N, int6
   B2_RETURN_IF_ERROR(device_info(&d));
   const int bn = tma_bn(N);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
-  int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);
+  int splits = splits_for(tiles, K, persistent_ctas(d), min_kb_per_split);
   int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
   if (kps < BK) kps = BK;
   splits = (int)ceil_div(K, kps);
@@ -590,7 +590,7 @@ int run_gemm(const AV& a, const BV& b, int64_t M, int64_t N, int64_t K, float* o
   }
   const int bn = choose_bn(N);
   const int64_t tiles = ceil_div(N, bn) * ceil_div(M, BM);
-  int splits = splits_for(tiles, K, d->sm_count, min_kb_per_split);
+  int splits = splits_for(tiles, K, persistent_ctas(d), min_kb_per_split);
   int64_t kps = ceil_div(ceil_div(K, splits), BK) * BK;
   if (kps < BK) kps = BK;
   splits = (int)(K > 0 ? ceil_div(K, kps) : 1);
