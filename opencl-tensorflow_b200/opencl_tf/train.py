@@ -136,7 +136,8 @@ class TrainStep:
     ``reserved_sms``: with more than one rank, SMs kept free of the library's
     persistent tensor-core kernels so that NCCL's all-reduce kernels run
     beside the backward pass instead of waiting for SMs (default: the
-    ``B2_RESERVED_SMS`` environment variable, else 0)."""
+    ``B2_RESERVED_SMS`` environment variable, else 0).  The gradient buckets
+    are about ``B2_BUCKET_BYTES`` (default 4 MiB) each."""
 
     def __init__(self, model: torch.nn.Module, lr: float = 1e-3, graphed: bool = True, warmup: int = 3,
                  group=None, reserved_sms: int | None = None):
@@ -144,7 +145,8 @@ class TrainStep:
         self.params = [p for p in model.parameters() if p.requires_grad]
         dev = self.params[0].device
         self.opt = Adam(self.params, learning_rate=lr)
-        self.avg = GradientAverager(self.params, group)
+        bucket = int(os.environ.get("B2_BUCKET_BYTES", str(4 << 20)))
+        self.avg = GradientAverager(self.params, group, bucket_bytes=bucket)
         if self.avg.world > 1 and dev.type == "cuda":
             if reserved_sms is None:
                 reserved_sms = int(os.environ.get("B2_RESERVED_SMS", "0"))
