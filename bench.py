@@ -310,35 +310,39 @@ def run_ours(args, rank, world, local_rank):
     clocks.start()
     time.sleep(0.3)
     torch.cuda.nvtx.range_push("timed_steps")
-    ms_dev = timed(lambda: step(x_dev, t_dev), args.steps)
+    # the batch is already in HBM: in the graph's own input buffers (the
+    # capture copied x_dev / t_dev there), so a step is the graph replay alone
+    ms_dev = timed(lambda: step(step.static_x, step.static_y), args.steps)
     torch.cuda.nvtx.range_pop()
 
     # ---- end to end: pinned host batch in, loss out, every step.  Like an
     # input pipeline, the next step's batch is copied host->device on a copy
-    # stream while this step computes; each step's timed interval contains the
-    # complete copy of the next step's batch (step 0 also its own) and the
-    # device->host copy of its loss, so every byte crosses inside the timing.
+    # stream while this step computes -- straight into the input buffers of
+    # the captured graph that will run it (two graphs of the step alternate);
+    # each step's timed interval contains the complete copy of the next
+    # step's batch (step 0 also its own) and the device->host copy of its
+    # loss, so every byte crosses inside the timing.
     x_host = torch.from_numpy(x_np).pin_memory()
     t_host = torch.from_numpy(t_np).pin_memory()
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
     copy_stream = torch.cuda.Stream(dev)
-    stage_x = [torch.empty_like(x_dev) for _ in range(2)]
-    stage_t = [torch.empty_like(t_dev) for _ in range(2)]
+    slots = [step.graph_inputs(0), step.graph_inputs(1)]
+    torch.cuda.synchronize(dev)
 
     def e2e_timed(K):
         cs = torch.cuda.current_stream(dev)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
         ready = [torch.cuda.Event() for _ in range(K)]
-        consumed = [torch.cuda.Event() for _ in range(K)]
+        done = [torch.cuda.Event() for _ in range(K)]
 
         def h2d(j, after):
             with torch.cuda.stream(copy_stream):
                 copy_stream.wait_event(after)
                 if j >= 2:
-                    copy_stream.wait_event(consumed[j - 2])  # stage j % 2 was read by step j - 2
-                stage_x[j % 2].copy_(x_host, non_blocking=True)
-                stage_t[j % 2].copy_(t_host, non_blocking=True)
+                    copy_stream.wait_event(done[j - 2])  # graph j % 2 finished step j - 2
+                slots[j % 2][0].copy_(x_host, non_blocking=True)
+                slots[j % 2][1].copy_(t_host, non_blocking=True)
                 ready[j].record(copy_stream)
 
         barrier()
@@ -350,10 +354,8 @@ def run_ours(args, rank, world, local_rank):
             if i + 1 < K:
                 h2d(i + 1, starts[i])
             cs.wait_event(ready[i])
-            step.static_x.copy_(stage_x[i % 2], non_blocking=True)
-            step.static_y.copy_(stage_t[i % 2], non_blocking=True)
-            consumed[i].record(cs)
-            loss = step(step.static_x, step.static_y)
+            loss = step.replay(i % 2)
+            done[i].record(cs)
             loss_host.copy_(loss, non_blocking=True)
             if i + 1 < K:
                 cs.wait_event(ready[i + 1])
@@ -375,8 +377,8 @@ def run_ours(args, rank, world, local_rank):
     with torch.cuda.stream(copy_stream):
         h_s.record(copy_stream)
         for _ in range(5):
-            stage_x[0].copy_(x_host, non_blocking=True)
-            stage_t[0].copy_(t_host, non_blocking=True)
+            slots[0][0].copy_(x_host, non_blocking=True)
+            slots[0][1].copy_(t_host, non_blocking=True)
         h_e.record(copy_stream)
     torch.cuda.synchronize(dev)
     h2d_ms = h_s.elapsed_time(h_e) / 5
@@ -417,8 +419,9 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(x_host.numel() * 4 + t_host.numel() * 4), "d2h_bytes_per_step": 4,
                 "ms_per_step": round(ms_e2e / args.steps, 4),
                 "h2d_ms_alone": round(h2d_ms, 4),
-                "pipeline": "next batch copied host->device on a copy stream during the step; each step's "
-                            "events enclose that copy and the loss read-back"},
+                "pipeline": "next batch copied host->device on a copy stream during the step, into the input "
+                            "buffers of the second captured graph of the step (two alternate); each step's events "
+                            "enclose that copy and the loss read-back"},
         "gpu_launches": int(per_step_launches * args.steps),
         "roofline": roof, "per_op": per_op, "cpu_baseline": cpu, "clocks": clk,
         "final_loss": round(loss_value, 6),

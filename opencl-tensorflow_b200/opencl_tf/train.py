@@ -155,6 +155,8 @@ class TrainStep:
         self.warmup = warmup
         self.graph = None
         self.static_x = self.static_y = self.static_loss = None
+        self.graph1 = None
+        self.static_x1 = self.static_y1 = self.static_loss1 = None
 
     def _eager(self, x, y):
         self.opt.zero_grad(set_to_none=True)
@@ -195,6 +197,38 @@ class TrainStep:
         self.graph.replay()
         return self.static_loss
 
+    def graph_inputs(self, slot: int):
+        """The static input buffers (x, y) of captured graph ``slot`` (0 or 1).
+        Graph 1 is the same step captured on a second pair of buffers, so an
+        input pipeline can copy the next batch straight into the buffers of
+        the graph that will run it while the other graph runs (no staging
+        copy inside the step).  Graph 0 must have been captured (one call)."""
+        if self.graph is None:
+            raise RuntimeError("run the step once before asking for its graph inputs")
+        if slot == 0:
+            return self.static_x, self.static_y
+        if self.graph1 is None:
+            self.static_x1 = torch.empty_like(self.static_x)
+            self.static_y1 = torch.empty_like(self.static_y)
+            self.static_x1.copy_(self.static_x)
+            self.static_y1.copy_(self.static_y)
+            torch.cuda.current_stream(self.static_x.device).synchronize()
+            self.graph1 = torch.cuda.CUDAGraph()
+            self.opt.zero_grad(set_to_none=True)
+            with torch.cuda.graph(self.graph1):
+                self.static_loss1 = self._eager(self.static_x1, self.static_y1)
+        return self.static_x1, self.static_y1
+
+    def replay(self, slot: int) -> torch.Tensor:
+        """One step on graph ``slot``'s input buffers; returns its loss (a
+        device scalar)."""
+        if slot == 0:
+            self.graph.replay()
+            return self.static_loss
+        self.graph1.replay()
+        return self.static_loss1
+
     def release(self) -> None:
-        """Drop the captured graph (before destroying a process group)."""
+        """Drop the captured graphs (before destroying a process group)."""
         self.graph = None
+        self.graph1 = None

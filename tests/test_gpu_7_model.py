@@ -196,3 +196,31 @@ def test_fused_bn_relu_model_matches_unfused(otf):
         assert torch.equal(a.grad, b.grad), n
     for (n, a), (_, b) in zip(fused.named_buffers(), plain.named_buffers()):
         assert torch.equal(a, b), n
+
+
+def test_second_graph_equals_first(otf):
+    """Two captured graphs of the step (graph 1 on its own input buffers, for an
+    input pipeline) compute the same training steps: alternating them gives
+    the same parameters, bit for bit, as replaying graph 0 only."""
+    from opencl_tf.train import TrainStep
+    batches = [_batch(8, seed=20 + i) for i in range(5)]
+    m0, m1 = _model(9), _model(9)
+    s0 = TrainStep(m0, graphed=True, warmup=3)
+    s1 = TrainStep(m1, graphed=True, warmup=3)
+    x, t = batches[0]
+    xd, td = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
+    s0(xd, td)
+    s1(xd, td)  # both: warm-up steps + the capture of graph 0
+    for i, (x, t) in enumerate(batches[1:]):
+        xd, td = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
+        l0 = s0(xd, td)
+        bx, by = s1.graph_inputs(i % 2)
+        bx.copy_(xd)
+        by.copy_(td)
+        l1 = s1.replay(i % 2)
+        torch.cuda.synchronize()
+        assert torch.equal(l0, l1), i
+    for a, b in zip(m0.parameters(), m1.parameters()):
+        assert torch.equal(a, b)
+    s0.release()
+    s1.release()
