@@ -68,6 +68,7 @@ class GradientAverager:
                 self.buckets.append(cur)
             self.bucket_of = {p: b for b, ps in enumerate(self.buckets) for p in ps}
             self.comm = torch.cuda.Stream(device=self.params[0].device)
+            self.done = [torch.cuda.Event() for _ in self.buckets]
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._grad_ready)
 
@@ -94,7 +95,21 @@ class GradientAverager:
             with c10d._coalescing_manager(self.group, dev):
                 for g in grads:
                     dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+            self.done[b].record(self.comm)
         self.launched += 1
+
+    def wait_buckets(self, buckets) -> None:
+        """Make the current stream wait for the all-reduces of ``buckets``
+        (indices into ``self.buckets``) of the armed backward pass only, so
+        work on their parameters can start while later buckets are still in
+        flight.  Calling the averager afterwards still joins every bucket."""
+        if not self.armed:
+            return
+        if self.launched != len(self.buckets):
+            raise RuntimeError("a parameter has no gradient; every rank must produce every gradient")
+        cur = torch.cuda.current_stream(self.params[0].device)
+        for b in buckets:
+            cur.wait_event(self.done[b])
 
     def __call__(self) -> None:
         if self.world == 1:
@@ -144,9 +159,19 @@ class TrainStep:
         self.model = model
         self.params = [p for p in model.parameters() if p.requires_grad]
         dev = self.params[0].device
-        self.opt = Adam(self.params, learning_rate=lr)
         bucket = int(os.environ.get("B2_BUCKET_BYTES", str(4 << 20)))
         self.avg = GradientAverager(self.params, group, bucket_bytes=bucket)
+        # With overlapped buckets the last bucket's all-reduce can only start
+        # after the last gradient of backward (the stem's); Adam over every
+        # other parameter runs beside it, Adam over that bucket after it.  Two
+        # optimizers, each with its own step counter (always equal), apply
+        # exactly Keras's update to each parameter.
+        if self.avg.overlap and len(self.avg.buckets) > 1:
+            late = {id(p) for p in self.avg.buckets[-1]}
+            self.opts = [Adam([p for p in self.params if id(p) not in late], learning_rate=lr),
+                         Adam([p for p in self.params if id(p) in late], learning_rate=lr)]
+        else:
+            self.opts = [Adam(self.params, learning_rate=lr)]
         if self.avg.world > 1 and dev.type == "cuda":
             if reserved_sms is None:
                 reserved_sms = int(os.environ.get("B2_RESERVED_SMS", "0"))
@@ -158,13 +183,23 @@ class TrainStep:
         self.graph1 = None
         self.static_x1 = self.static_y1 = self.static_loss1 = None
 
+    def zero_grad(self) -> None:
+        for o in self.opts:
+            o.zero_grad(set_to_none=True)
+
     def _eager(self, x, y):
-        self.opt.zero_grad(set_to_none=True)
+        self.zero_grad()
         loss = mse(self.model(x, training=True), y)
         self.avg.begin()
         loss.backward()
-        self.avg()
-        self.opt.step()
+        if len(self.opts) == 2:
+            self.avg.wait_buckets(range(len(self.avg.buckets) - 1))
+            self.opts[0].step()
+            self.avg()
+            self.opts[1].step()
+        else:
+            self.avg()
+            self.opts[0].step()
         return loss.detach()
 
     def _capture(self, x, y):
@@ -179,7 +214,7 @@ class TrainStep:
                 self._eager(self.static_x, self.static_y)
         torch.cuda.current_stream(x.device).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
-        self.opt.zero_grad(set_to_none=True)
+        self.zero_grad()
         with torch.cuda.graph(self.graph):
             self.static_loss = self._eager(self.static_x, self.static_y)
 
@@ -214,7 +249,7 @@ class TrainStep:
             self.static_y1.copy_(self.static_y)
             torch.cuda.current_stream(self.static_x.device).synchronize()
             self.graph1 = torch.cuda.CUDAGraph()
-            self.opt.zero_grad(set_to_none=True)
+            self.zero_grad()
             with torch.cuda.graph(self.graph1):
                 self.static_loss1 = self._eager(self.static_x1, self.static_y1)
         return self.static_x1, self.static_y1

@@ -72,8 +72,30 @@ def _worker(rank, world, port, q):
         dist.all_gather(other, flat)
         same = all(torch.equal(other[0], o) for o in other)
         step.release()
+        # 3) the step's optimizer is split in two (Adam over the parameters
+        # whose all-reduce is done runs beside the last bucket's all-reduce):
+        # the parameters equal one Adam over all of them, bit for bit
+        from opencl_tf.optimizers import Adam
+        torch.manual_seed(0)
+        m1 = build_model(device=dev)
+        torch.manual_seed(0)
+        m2 = build_model(device=dev)
+        s1 = TrainStep(m1, graphed=False)
+        assert len(s1.opts) == 2
+        avg2 = GradientAverager(m2.parameters())
+        opt2 = Adam(list(m2.parameters()))
+        for _ in range(2):
+            s1(x, t)
+            opt2.zero_grad()
+            l2 = mse(m2(x, training=True), t)
+            avg2.begin()
+            l2.backward()
+            avg2()
+            opt2.step()
+        torch.cuda.synchronize()
+        split_same = all(torch.equal(a, b) for a, b in zip(m1.parameters(), m2.parameters()))
         dist.destroy_process_group()
-        q.put((rank, err, same, float(loss)))
+        q.put((rank, err, same and split_same, float(loss)))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e), False, 0.0))
 
