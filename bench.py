@@ -236,9 +236,9 @@ def cpu_reference_steps(widened, sample_images, steps, warmup, min_seconds=0.0, 
 # one ncu capture of that workload; keyed by op and its algorithmic bytes so a
 # different workload reports null.  Source: the named summary under profiles/.
 NCU_TRAFFIC = {
-    ("conv2d_backprop_filter", 113258304): (118519552, "profiles/tma_gemm_conv_wgrad_readme_stem.md"),
+    ("conv2d_backprop_filter", 113258304): (118956288, "profiles/tma_gemm_conv_wgrad_readme_stem.md"),
     ("depthwise_conv2d_backprop_filter", 125830848): (132687360, "profiles/dw_wgrad_staged_readme_dsconv1.md"),
-    ("batch_norm_relu_grad", 301991040): (474196736, "profiles/bn_relu_grad_op_readme_stem.md"),
+    ("batch_norm_relu_grad", 301991040): (469819136, "profiles/bn_relu_grad_op_readme_stem.md"),
 }
 
 
