@@ -66,17 +66,31 @@ class GradientAverager:
                     cur, nbytes = [], 0
             if cur:
                 self.buckets.append(cur)
+            # The first parameter's gradient comes last out of backward (the
+            # first layer's weight): alone in the last bucket, it does not hold
+            # back the exchange of the other small gradients, which then runs
+            # while that gradient is computed.
+            if len(self.buckets[-1]) > 1:
+                self.buckets[-1], first = self.buckets[-1][:-1], self.buckets[-1][-1:]
+                self.buckets.append(first)
             self.bucket_of = {p: b for b, ps in enumerate(self.buckets) for p in ps}
             self.comm = torch.cuda.Stream(device=self.params[0].device)
             self.done = [torch.cuda.Event() for _ in self.buckets]
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._grad_ready)
+        # Called on the communication stream once every bucket but the last
+        # has been launched (before the last one), e.g. the optimizer step of
+        # the parameters whose gradients are then final; early_ran tells
+        # whether it ran in the current backward pass.
+        self.early_hook = None
+        self.early_ran = False
 
     def begin(self) -> None:
         """Arm the overlapped reduction for the next backward pass."""
         if self.overlap:
             self.ready = [0] * len(self.buckets)
             self.launched = 0
+            self.early_ran = False
             self.armed = True
 
     def _grad_ready(self, p) -> None:
@@ -96,7 +110,12 @@ class GradientAverager:
                 for g in grads:
                     dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
             self.done[b].record(self.comm)
-        self.launched += 1
+            self.launched += 1
+            last = len(self.buckets) - 1
+            if (self.early_hook is not None and self.launched == last and b != last
+                    and self.ready[last] < len(self.buckets[last])):
+                self.early_hook()
+                self.early_ran = True
 
     def wait_buckets(self, buckets) -> None:
         """Make the current stream wait for the all-reduces of ``buckets``
@@ -149,9 +168,10 @@ class TrainStep:
     """fwd + MSE + bwd + gradient averaging + Adam for ``model`` on (x, y).
 
     ``reserved_sms``: with more than one rank, SMs kept free of the library's
-    persistent tensor-core kernels so that NCCL's all-reduce kernels run
-    beside the backward pass instead of waiting for SMs (default: the
-    ``B2_RESERVED_SMS`` environment variable, else 0).  The gradient buckets
+    persistent tensor-core kernels so that NCCL's all-reduce kernels (and the
+    early optimizer step) run beside the backward pass's last kernel, the
+    stem filter gradient, instead of waiting for it (default: the
+    ``B2_RESERVED_SMS`` environment variable, else 4).  The gradient buckets
     are about ``B2_BUCKET_BYTES`` (default 4 MiB) each."""
 
     def __init__(self, model: torch.nn.Module, lr: float = 1e-3, graphed: bool = True, warmup: int = 3,
@@ -162,19 +182,25 @@ class TrainStep:
         bucket = int(os.environ.get("B2_BUCKET_BYTES", str(4 << 20)))
         self.avg = GradientAverager(self.params, group, bucket_bytes=bucket)
         # With overlapped buckets the last bucket's all-reduce can only start
-        # after the last gradient of backward (the stem's); Adam over every
-        # other parameter runs beside it, Adam over that bucket after it.  Two
-        # optimizers, each with its own step counter (always equal), apply
-        # exactly Keras's update to each parameter.
+        # after the last gradient of backward (the first layer's weight); Adam
+        # over every other parameter runs on the communication stream as soon
+        # as their buckets are exchanged (beside the backward pass's last
+        # kernels), Adam over the last bucket after it.  Two optimizers, each
+        # with its own step counter (always equal), apply exactly Keras's
+        # update to each parameter.
         if self.avg.overlap and len(self.avg.buckets) > 1:
             late = {id(p) for p in self.avg.buckets[-1]}
             self.opts = [Adam([p for p in self.params if id(p) not in late], learning_rate=lr),
                          Adam([p for p in self.params if id(p) in late], learning_rate=lr)]
+            # on a stream of its own, right after the other buckets' exchange
+            # (so the last bucket's all-reduce does not queue behind it)
+            self.opt_stream = torch.cuda.Stream(device=dev)
+            self.avg.early_hook = self._early_step
         else:
             self.opts = [Adam(self.params, learning_rate=lr)]
         if self.avg.world > 1 and dev.type == "cuda":
             if reserved_sms is None:
-                reserved_sms = int(os.environ.get("B2_RESERVED_SMS", "0"))
+                reserved_sms = int(os.environ.get("B2_RESERVED_SMS", "4"))
             set_reserved_sms(reserved_sms)
         self.graphed = graphed and dev.type == "cuda"
         self.warmup = warmup
@@ -182,6 +208,12 @@ class TrainStep:
         self.static_x = self.static_y = self.static_loss = None
         self.graph1 = None
         self.static_x1 = self.static_y1 = self.static_loss1 = None
+
+    def _early_step(self) -> None:
+        # called with the communication stream current
+        self.opt_stream.wait_stream(self.avg.comm)
+        with torch.cuda.stream(self.opt_stream):
+            self.opts[0].step()
 
     def zero_grad(self) -> None:
         for o in self.opts:
@@ -193,9 +225,12 @@ class TrainStep:
         self.avg.begin()
         loss.backward()
         if len(self.opts) == 2:
-            self.avg.wait_buckets(range(len(self.avg.buckets) - 1))
-            self.opts[0].step()
+            if not self.avg.early_ran:  # the last bucket was not the last to complete
+                self.avg.wait_buckets(range(len(self.avg.buckets) - 1))
+                self.opts[0].step()
             self.avg()
+            if self.avg.early_ran:
+                torch.cuda.current_stream(x.device).wait_stream(self.opt_stream)
             self.opts[1].step()
         else:
             self.avg()
