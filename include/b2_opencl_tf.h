@@ -384,6 +384,30 @@ int b2_adam_update(b2_stream_t stream, int num_tensors, float* const* params,
  * nonzero count means a kernel gave up waiting and its output is invalid. */
 int b2_device_timeouts(unsigned int* count);
 
+/* ---- Gradient exchange over NVLink peer memory (data parallelism) --------
+ * No reference op: the reference trains on one device.  Averages a small
+ * fp32 tensor across the `world` ranks (GPUs of one node, one process each)
+ * in one kernel per rank: each rank stores its copy into every rank's
+ * exchange block, raises a flag there, waits (bounded: an expired wait makes
+ * later calls return B2_ERR_TIMEOUT) for every rank's flag and adds the copies
+ * in rank order, so every rank gets the same bits.  Every rank must make the
+ * same calls in the same order.
+ *
+ * Setup, once per rank: b2_peer_buffer_create(b2_peer_exchange_bytes(n,
+ * world)) gives this rank's block and a 64-byte handle; the handles are
+ * exchanged between the processes (any host channel), and each rank maps the
+ * others' blocks with b2_peer_buffer_open.  peer_blocks[r] is rank r's block
+ * as mapped in the calling process (its own block at [rank]); counters: two
+ * zeroed uint32 of device memory per rank (call epoch and a ticket). */
+size_t b2_peer_exchange_bytes(int64_t n, int world);
+int b2_peer_buffer_create(size_t bytes, void** ptr, unsigned char handle[64]);
+int b2_peer_buffer_open(const unsigned char handle[64], void** ptr);
+int b2_peer_buffer_close(void* peer_ptr);
+int b2_peer_buffer_free(void* ptr);
+int b2_peer_allreduce_avg(b2_stream_t stream, float* data, int64_t n, int rank,
+                          int world, void* const* peer_blocks,
+                          unsigned int* counters);
+
 /* ---- Device-side wait failures as op errors ------------------------------
  * The reference turns every device failure into a TF status
  * (OP_REQUIRES_CL -> errors::Internal, src/ops/conv2d_ops.cc:43-45).  Here

@@ -28,7 +28,8 @@
 #include "tma_gemm.cuh"
 
 namespace b2 {
-unsigned int dw_timeouts();  // depthwise.cu
+unsigned int dw_timeouts();    // depthwise.cu
+unsigned int peer_timeouts();  // peer_exchange.cu
 
 namespace tc {
 
@@ -851,7 +852,7 @@ int b2_dense_backprop_bias(b2_stream_t stream, const float* grad_y, const int64_
 int b2_device_timeouts(unsigned int* count) {
   clear_error();
   B2_CUDA_OR_RETURN(cudaMemcpyFromSymbol(count, g_tc_timeouts, sizeof(unsigned int)));
-  *count += b2::dw_timeouts();
+  *count += b2::dw_timeouts() + b2::peer_timeouts();
   return B2_OK;
 }
 

@@ -97,6 +97,16 @@ for _name, _args in _SIGS.items():
     _fn.restype = _I
 _lib.b2_last_error.restype = ctypes.c_char_p
 _lib.b2_last_error.argtypes = []
+_U8P = ctypes.POINTER(ctypes.c_ubyte)
+_VPP = ctypes.POINTER(ctypes.c_void_p)
+_lib.b2_peer_exchange_bytes.restype = ctypes.c_size_t
+_lib.b2_peer_exchange_bytes.argtypes = [_I64, _I]
+for _name, _args in {"b2_peer_buffer_create": [ctypes.c_size_t, _VPP, _U8P],
+                     "b2_peer_buffer_open": [_U8P, _VPP],
+                     "b2_peer_buffer_close": [_P], "b2_peer_buffer_free": [_P],
+                     "b2_peer_allreduce_avg": [_P, _P, _I64, _I, _I, _VPP, _P]}.items():
+    getattr(_lib, _name).argtypes = _args
+    getattr(_lib, _name).restype = _I
 
 
 class PoolStats(ctypes.Structure):

@@ -23,6 +23,10 @@ import torch
 import torch.distributed as dist
 from torch.distributed import distributed_c10d as c10d
 
+import ctypes
+import socket
+
+from . import _library as _L
 from ._library import set_reserved_sms, step_ops
 from .optimizers import Adam
 
@@ -31,6 +35,86 @@ def mse(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     """Keras "mse" of the batch as a device scalar: one kernel forward, one
     backward (``step_ops.opencl_mse_loss``)."""
     return step_ops.opencl_mse_loss(pred, target)
+
+
+class PeerExchange:
+    """Averages an fp32 tensor of ``n`` elements in place across the ranks of
+    ``group`` -- GPUs of one node, one process each -- over NVLink peer memory
+    (``b2_peer_allreduce_avg``: one kernel per rank stores its copy into every
+    rank's exchange block and adds the copies in rank order after every
+    rank's flag, so all ranks get the same bits).  Setup is collective: every
+    rank allocates its block, the CUDA IPC handles go through the process
+    group, each rank maps the others' blocks.  ``PeerExchange.create`` returns
+    None on every rank unless every rank could set it up."""
+
+    def __init__(self, n: int, group, device):
+        self.n = int(n)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.own = None
+        self.opened = []
+        size = _L._lib.b2_peer_exchange_bytes(self.n, self.world)
+        if size == 0:
+            raise RuntimeError("peer exchange: unsupported size or world")
+        own, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+        with torch.cuda.device(device):
+            _L._check(_L._lib.b2_peer_buffer_create(size, ctypes.byref(own), handle))
+        self.own = own.value
+        self._handle = bytes(handle)
+        self.device = device
+        self.counters = torch.zeros(2, dtype=torch.int32, device=device)
+
+    def _open(self, handles) -> None:
+        bases = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self.own)
+                    continue
+                p = ctypes.c_void_p()
+                _L._check(_L._lib.b2_peer_buffer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(p)))
+                self.opened.append(p.value)
+                bases.append(p.value)
+        self.bases = (ctypes.c_void_p * self.world)(*bases)
+
+    @classmethod
+    def create(cls, n: int, group, device):
+        world = dist.get_world_size(group)
+        ex, err = None, ""
+        try:
+            ex = cls(n, group, device)
+        except Exception as e:  # noqa: BLE001 -- agreed on below
+            err = repr(e)
+        info = [None] * world
+        mine = (socket.gethostname(), ex._handle if ex is not None else None, err)
+        dist.all_gather_object(info, mine, group=group)
+        ok = all(h is not None for _, h, _ in info) and len({host for host, _, _ in info}) == 1 and world <= 8
+        if ok:
+            try:
+                ex._open([h for _, h, _ in info])
+            except Exception:  # noqa: BLE001
+                ok = False
+        flags = [None] * world
+        dist.all_gather_object(flags, ok, group=group)
+        if all(flags):
+            return ex
+        if ex is not None:
+            ex.close()
+        return None
+
+    def __call__(self, t: torch.Tensor) -> None:
+        """Average ``t`` (contiguous fp32, n elements) on the current stream."""
+        _L._check(_L._lib.b2_peer_allreduce_avg(_L._stream(t), _L._p(t), self.n, self.rank, self.world, self.bases,
+                                                _L._p(self.counters)))
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            for p in self.opened:
+                _L._lib.b2_peer_buffer_close(p)
+            if self.own is not None:
+                _L._lib.b2_peer_buffer_free(self.own)
+        self.opened, self.own = [], None
 
 
 class GradientAverager:
@@ -76,6 +160,14 @@ class GradientAverager:
             self.bucket_of = {p: b for b, ps in enumerate(self.buckets) for p in ps}
             self.comm = torch.cuda.Stream(device=self.params[0].device)
             self.done = [torch.cuda.Event() for _ in self.buckets]
+            # The last bucket (one small tensor, always exposed) goes over
+            # NVLink peer memory instead of a latency-bound NCCL ring when all
+            # ranks share a node (B2_PEER_EXCHANGE=0 turns this off).
+            self.peer = None
+            last = self.buckets[-1]
+            if (len(last) == 1 and last[0].dtype == torch.float32 and last[0].numel() <= (1 << 22)
+                    and os.environ.get("B2_PEER_EXCHANGE", "1") != "0"):
+                self.peer = PeerExchange.create(last[0].numel(), group, last[0].device)
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._grad_ready)
         # Called on the communication stream once every bucket but the last
@@ -106,9 +198,14 @@ class GradientAverager:
         dev = grads[0].device
         self.comm.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.comm):
-            with c10d._coalescing_manager(self.group, dev):
-                for g in grads:
-                    dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+            if self.peer is not None and b == len(self.buckets) - 1:
+                if not grads[0].is_contiguous():
+                    raise RuntimeError("peer exchange needs a contiguous gradient")
+                self.peer(grads[0])
+            else:
+                with c10d._coalescing_manager(self.group, dev):
+                    for g in grads:
+                        dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
             self.done[b].record(self.comm)
             self.launched += 1
             last = len(self.buckets) - 1
@@ -116,6 +213,14 @@ class GradientAverager:
                     and self.ready[last] < len(self.buckets[last])):
                 self.early_hook()
                 self.early_ran = True
+
+    def close(self) -> None:
+        """Unmap and free the peer-exchange blocks (after the last step, before
+        the process group goes)."""
+        if getattr(self, "peer", None) is not None:
+            torch.cuda.synchronize(self.peer.device)
+            self.peer.close()
+            self.peer = None
 
     def wait_buckets(self, buckets) -> None:
         """Make the current stream wait for the all-reduces of ``buckets``
@@ -299,6 +404,8 @@ class TrainStep:
         return self.static_loss1
 
     def release(self) -> None:
-        """Drop the captured graphs (before destroying a process group)."""
+        """Drop the captured graphs and the peer-exchange mappings (before
+        destroying a process group)."""
         self.graph = None
         self.graph1 = None
+        self.avg.close()
