@@ -99,6 +99,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Three independent non-blocking probes in one asm block: their
+// shared-memory round trips overlap instead of queueing one after the other
+// behind other warps' shared-memory traffic.  Bit i of the result: barrier i
+// has completed the phase of its parity.
+__device__ __forceinline__ uint32_t mbar_probe3(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2,
+                                                uint32_t p2) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred q0, q1, q2;\n\t.reg .b32 t0, t1, t2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q0, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q1, [%3], %4;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q2, [%5], %6;\n\t"
+      "selp.b32 t0, 1, 0, q0;\n\t"
+      "selp.b32 t1, 2, 0, q1;\n\t"
+      "selp.b32 t2, 4, 0, q2;\n\t"
+      "or.b32 t0, t0, t1;\n\t"
+      "or.b32 %0, t0, t2;\n\t}"
+      : "=r"(r)
+      : "r"(smem_u32(b0)), "r"(p0), "r"(smem_u32(b1)), "r"(p1), "r"(smem_u32(b2)), "r"(p2)
+      : "memory");
+  return r;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -742,31 +742,46 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       uint32_t it = 0, g = 0;  // g counts chunks
       uint32_t sq = 0, lap_q = 0;  // it = lap_q * Q + sq
       bool ok = !(bres && blockIdx.x < tiles) || mbar_wait(b_ready, 0, ws);
-      for (int64_t t = blockIdx.x; t < tiles && ok && !aborted(ws); t += gridDim.x) {
-        const TmaTile tc = tma_tile(p, t);
-        for (int kb0 = 0; kb0 < tc.nkb && ok; kb0 += kChunkKB, ++g) {
+      // With one split every tile has the same k-blocks: no tile decomposition
+      // on this thread's path (an abort is seen by the waits, which check it).
+      const int nkb_all = p.splits == 1 ? (int)((p.K + BK - 1) / BK) : -1;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int tile_nkb = nkb_all >= 0 ? nkb_all : tma_tile(p, t).nkb;
+        for (int kb0 = 0; kb0 < tile_nkb && ok; kb0 += kChunkKB, ++g) {
           const int a = (int)(g & 1u);
           const uint32_t use = g >> 1;
-          if (use > 0 && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, ws)) {
+          const int kb1 = kb0 + kChunkKB < tile_nkb ? kb0 + kChunkKB : tile_nkb;
+          // Every barrier operation of this thread queues behind the other
+          // warps' shared-memory traffic, so the accumulator and the next two
+          // operand stages are probed together (their round trips overlap);
+          // only what is not complete yet is waited for.  A stage's previous
+          // phase is one this thread consumed, so a completed parity can only
+          // mean the current use.
+          uint32_t sq1 = sq + 1 == Q ? 0u : sq + 1, lap1 = sq + 1 == Q ? lap_q + 1 : lap_q;
+          uint32_t ready = mbar_probe3(&chunk_empty[a], (use - 1) & 1u, &op_full[sq], lap_q & 1u, &op_full[sq1],
+                                       lap1 & 1u);
+          if (use > 0 && !(ready & 1u) && !mbar_wait(&chunk_empty[a], (use - 1) & 1u, ws)) {
             ok = false;
             break;
           }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t d = tmem_base + (uint32_t)a * acc_cols;
-          const int kb1 = kb0 + kChunkKB < tc.nkb ? kb0 + kChunkKB : tc.nkb;
+          bool first = true;
           for (int kb = kb0; kb < kb1 && ok;) {
-            // The wait and the thread-sync fence stall this thread for about
-            // as long as four MMAs take, so when the next operand stage is
-            // ready too (converters usually run ahead), both k-blocks are
-            // issued behind one fence.  The stage after sq is tested without
-            // blocking; its previous phase is one this thread consumed, so a
-            // completed parity can only mean the current use.
-            if (!mbar_wait(&op_full[sq], lap_q & 1u, ws)) {
+            // One wait and one thread-sync fence (which also covers the
+            // accumulator's release at a chunk's start) for a pair of
+            // k-blocks when the second stage is ready too.
+            if (!first) {
+              sq1 = sq + 1 == Q ? 0u : sq + 1;
+              lap1 = sq + 1 == Q ? lap_q + 1 : lap_q;
+              // bits 1 and 2 as at the chunk's start (bit 0 repeats bit 1)
+              ready = mbar_probe3(&op_full[sq], lap_q & 1u, &op_full[sq], lap_q & 1u, &op_full[sq1], lap1 & 1u);
+            }
+            first = false;
+            if (!(ready & 2u) && !mbar_wait(&op_full[sq], lap_q & 1u, ws)) {
               ok = false;
               break;
             }
-            const uint32_t sq1 = sq + 1 == Q ? 0u : sq + 1, lap1 = sq + 1 == Q ? lap_q + 1 : lap_q;
-            const int nkb = (kb + 1 < kb1 && mbar_try_wait(&op_full[sq1], lap1 & 1u)) ? 2 : 1;
+            const int nkb = (kb + 1 < kb1 && (ready & 4u)) ? 2 : 1;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             for (int u = 0; u < nkb; ++u, ++kb, ++it) {
               const uint32_t a_hi = tmem_base + a_col0 + sq * kASlotCols, a_lo = a_hi + BK;
