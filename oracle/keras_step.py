@@ -1,5 +1,5 @@
 """TEST INFRASTRUCTURE (oracle). The training step's loss and optimizer as
-Keras defines them, restated in numpy -- the checker for the device loss and
+Keras defines them, restated in numpy -- the oracle for the device loss and
 Adam kernels, never called by the product path.
 
 The reference trains with ``model.compile(optimizer=tf.keras.optimizers.Adam(

@@ -1,8 +1,8 @@
 """TEST INFRASTRUCTURE -- the parity oracle for the seven ops.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
-leg import this module.  It is the checker, never the thing measured on the
-GPU path and never a fallback for it.
+leg import this module.  It is what the GPU results are compared with,
+never the thing measured on the GPU path and never a fallback for it.
 
 Three arbiters, all on host numpy arrays:
 
