@@ -37,6 +37,27 @@ def mse(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     return step_ops.opencl_mse_loss(pred, target)
 
 
+def plan_buckets(nbytes, bucket_bytes: int = 4 << 20):
+    """Gradient buckets for parameters of ``nbytes`` (in the model's order):
+    lists of parameter indices, in the order backward produces the gradients
+    (reverse), each closed once it holds ``bucket_bytes``; the first parameter
+    (the first layer's weight, whose gradient comes last) gets a bucket of its
+    own, so it does not hold back the exchange of the others."""
+    buckets, cur, size = [], [], 0
+    for i in reversed(range(len(nbytes))):
+        cur.append(i)
+        size += int(nbytes[i])
+        if size >= bucket_bytes:
+            buckets.append(cur)
+            cur, size = [], 0
+    if cur:
+        buckets.append(cur)
+    if buckets and len(buckets[-1]) > 1:
+        buckets[-1], first = buckets[-1][:-1], buckets[-1][-1:]
+        buckets.append(first)
+    return buckets
+
+
 class PeerExchange:
     """Averages an fp32 tensor of ``n`` elements in place across the ranks of
     ``group`` -- GPUs of one node, one process each -- over NVLink peer memory
@@ -141,22 +162,8 @@ class GradientAverager:
         self.armed = False
         self.overlap = bool(overlap) and self.world > 1 and bool(self.params) and self.params[0].is_cuda
         if self.overlap:
-            self.buckets, cur, nbytes = [], [], 0
-            for p in reversed(self.params):
-                cur.append(p)
-                nbytes += p.numel() * p.element_size()
-                if nbytes >= bucket_bytes:
-                    self.buckets.append(cur)
-                    cur, nbytes = [], 0
-            if cur:
-                self.buckets.append(cur)
-            # The first parameter's gradient comes last out of backward (the
-            # first layer's weight): alone in the last bucket, it does not hold
-            # back the exchange of the other small gradients, which then runs
-            # while that gradient is computed.
-            if len(self.buckets[-1]) > 1:
-                self.buckets[-1], first = self.buckets[-1][:-1], self.buckets[-1][-1:]
-                self.buckets.append(first)
+            plan = plan_buckets([p.numel() * p.element_size() for p in self.params], bucket_bytes)
+            self.buckets = [[self.params[i] for i in b] for b in plan]
             self.bucket_of = {p: b for b, ps in enumerate(self.buckets) for p in ps}
             self.comm = torch.cuda.Stream(device=self.params[0].device)
             self.done = [torch.cuda.Event() for _ in self.buckets]

@@ -78,3 +78,32 @@ def test_missing_rank_times_out_on_the_host():
     out = q.get(timeout=120)
     p.join(30)
     assert out != "completed"
+
+
+def test_bucket_plan_matches_backward_order():
+    """The data-parallel step's buckets (opencl_tf/train.py: plan_buckets):
+    reverse parameter order, closed at the size threshold, the first
+    parameter alone in the last bucket.  The README model's parameter sizes
+    give three buckets: the Dense weight (9.4 MB) with its bias before it,
+    the other small parameters, and the stem filter."""
+    import importlib
+    sys.path.insert(0, str(ROOT / "opencl-tensorflow_b200"))
+    train = importlib.import_module("opencl_tf.train")
+    plan = train.plan_buckets
+    assert plan([]) == []
+    assert plan([100]) == [[0]]
+    assert plan([100, 200]) == [[1], [0]]
+    assert plan([8, 8, 8, 8], bucket_bytes=16) == [[3, 2], [1], [0]]
+    assert plan([8, 8, 8, 8], bucket_bytes=8) == [[3], [2], [1], [0]]
+    # the README network: stem kernel, BN gamma/beta, two blocks of
+    # (dw kernel, BN, pw kernel, BN), Dense W and b -- float32 bytes
+    sizes = [3 * 7 * 3 * 48, 48, 48,
+             9 * 48, 48, 48, 48 * 96, 96, 96,
+             9 * 96, 96, 96, 96 * 144, 144, 144,
+             18432 * 128, 128]
+    nbytes = [4 * n for n in sizes]
+    b = plan(nbytes)
+    assert b[0] == [16, 15]
+    assert b[-1] == [0]
+    assert b[1] == list(range(14, 0, -1))
+    assert sorted(i for bucket in b for i in bucket) == list(range(len(sizes)))
