@@ -11,20 +11,21 @@ after a few eager warm-up steps, so a step costs one graph launch instead of
 
 Data parallelism: with an initialised ``torch.distributed`` process group
 each rank runs the step on its own batch shard; the weight gradients are
-flattened into one bucket and averaged with a single all-reduce (NCCL over
-NVLink on GPUs) before the optimizer step.  BatchNorm statistics and moving
-averages stay per replica, as on one device in the reference.
+averaged in buckets while backward runs (in-place NCCL all-reduces over
+NVLink, the last small bucket over NVLink peer memory), and the optimizer
+step is split around the last bucket (``GradientAverager``, ``TrainStep``).
+BatchNorm statistics and moving averages stay per replica, as on one device
+in the reference.
 """
 from __future__ import annotations
 
+import ctypes
 import os
+import socket
 
 import torch
 import torch.distributed as dist
 from torch.distributed import distributed_c10d as c10d
-
-import ctypes
-import socket
 
 from . import _library as _L
 from ._library import set_reserved_sms, step_ops
