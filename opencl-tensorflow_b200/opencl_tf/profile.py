@@ -204,6 +204,43 @@ def stress_gemm(device=None, reps=10) -> dict:
     return out
 
 
+def _warm_step(batch: int, reps: int) -> int:
+    """Prints each kernel's device time per step of the README training step
+    replayed from its CUDA graph, L2 warm (as inside a training loop), from
+    CUPTI records of ``reps`` replays."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    from .model import build_model
+    from .train import TrainStep
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    model = build_model(device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.rand(batch, 64, 64, 3, device=dev, generator=g)
+    t = torch.rand(batch, 8, 8, 8, device=dev, generator=g)
+    step = TrainStep(model, graphed=True, warmup=3)
+    for _ in range(6):
+        step(x, t)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            step(x, t)
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0.0, 0])
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            agg[e.name][0] += getattr(e, "device_time_total", 0.0) or e.cuda_time_total
+            agg[e.name][1] += 1
+    total = sum(v[0] for v in agg.values())
+    print(f"kernel time per step: {total / reps:.1f} us over {reps} replays of the batch-{batch} step")
+    for name, (us, n) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
+        print(f"{us / reps:8.1f} us  {n // reps:3d}x  {name[:100]}")
+    step.release()
+    return 0
+
+
 def _cli() -> int:
     """Replay one op of a network's training step, e.g. for ncu:
 
@@ -226,7 +263,12 @@ def _cli() -> int:
     ap.add_argument("--model", choices=["build_model", "uwb_loc_v3"], default="build_model")
     ap.add_argument("--stress", choices=["forward", "backprop_input", "backprop_weight"],
                     help="run one pass of the 8192x4096x4096 stress GEMM instead")
+    ap.add_argument("--warm-step", action="store_true",
+                    help="per-kernel device time of the captured training step, warm (CUPTI through "
+                         "torch.profiler over --reps replays)")
     a = ap.parse_args()
+    if a.warm_step:
+        return _warm_step(a.batch, max(a.reps, 1))
     if a.stress:
         dev = torch.device("cuda", 0)
         x, w, b, dy = stress_gemm_inputs(dev)
