@@ -91,6 +91,27 @@ def test_no_alloc_matches_pooled_entry_point_two_calls(lib, shape):
         assert_close(outs[2].cpu().numpy(), v64, what="var vs float64")
 
 
+@pytest.mark.parametrize("shape", [(16, 32, 16, 48), (7, 5, 9, 6), (64, 32, 32, 256), (2, 8, 8, 4096),
+                                   (1, 4, 4, 16384)])
+def test_no_alloc_against_the_oracle(lib, port, shape):
+    """y, saved_mean and saved_var against the reference's BatchNorm kernels
+    (batchnorm_kernels.cl:35-80, in the oracle's bit-exact C restatement), at
+    the contract tolerance: the sums run in another order than the
+    reference's serial loop; y is then exact given the statistics."""
+    rng = np.random.default_rng(5)
+    C = shape[3]
+    x = (rng.standard_normal(shape) * 2 + 0.5).astype(np.float32)
+    g = (rng.standard_normal(C) + 1).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    y, mean, var = _run(lib, "b2_batch_norm_training_no_alloc", torch.from_numpy(x).cuda(),
+                        torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
+    torch.cuda.synchronize()
+    ry, rm, rv = port.batch_norm_training(x, g, b, 1e-3)
+    assert_close(mean.cpu().numpy(), rm, what="mean vs oracle")
+    assert_close(var.cpu().numpy(), rv, what="var vs oracle")
+    assert_close(y.cpu().numpy(), ry, what="y vs oracle")
+
+
 def test_no_alloc_rejects_too_many_channels(lib):
     x = torch.zeros(1, 1, 1, 16385, device="cuda")
     c = torch.zeros(16385, device="cuda")
